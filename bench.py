@@ -1,0 +1,438 @@
+"""Benchmark of the SunShape quantized-key decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c5]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU, NCCL)
+
+A step is one decode-attention pass over the whole synthetic KV cache of the
+workload (default ``c5``: batch 8, 64 query / 8 KV heads, head_dim 128, 128K
+context, block_dim 8, uint8 indices, bf16 values -- the 1/2/4/8-GPU config).
+With N GPUs the KV sequence is split evenly (strong scaling: total work fixed);
+each rank runs the fused kernel on its shard, the (max, sum, acc) partials are
+all-gathered over NCCL and merged.  Inputs (2.28 GB at N=1) are larger than the
+126 MB L2, so no flush is needed between steps.
+
+Prints ONE JSON line (rank 0).  ``value`` is whole-job KV tokens/s with inputs
+resident in HBM; ``e2e`` is the same metric through the public API
+(``SunShapeAttentionImpl.forward`` / ``KVShardedDecode``) with the step's query
+copied from pinned host memory and the output copied back inside the timed
+region.  ``--impl reference`` times the reference algorithm's CPU restatement
+(the oracle port; the reference itself is Python and does not travel to the GPU
+box) on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from sunshape_b200.workloads import CONFIGS, DecodeConfig, make_case  # noqa: E402
+
+METRIC = "KV tokens scored/s and HBM GB/s (% of peak), VQ decode attn, 1/2/4/8 B200"
+UNIT = "KV tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ----------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+# ----------------------------------------------------------------------------------- setup
+def build_shard(cfg: DecodeConfig, rank: int, world: int, dev: torch.device, seed: int = 0):
+    """Codec, encoded indices (+heavy) and values of this rank's KV shard; full queries."""
+    from sunshape_b200.codec import SunShapeBlockCodec
+    from sunshape_b200.distributed import kv_shard_bounds
+
+    case = make_case(cfg.with_(seq_len=min(cfg.seq_len, 8192)), device=dev, seed=seed)   # codebooks + perm
+    mode = "profileperm_mixed_precision" if cfg.n_heavy else "profileperm_baseline"
+    codec = SunShapeBlockCodec(cfg.head_dim, cfg.block_dim, cfg.n_centroids, mode=mode, device=dev,
+                               kv_heads=cfg.kv_heads)
+    codec.permutation.copy_(case["perm"])
+    codec.inv_permutation.copy_(case["inv_perm"])
+    codec.centroids.copy_(case["centroids"])
+    codec.mixed_high_precision_blocks.copy_(case["heavy_mask"])
+    codec.invalidate()
+    a, b = kv_shard_bounds(cfg.seq_len, world, rank)
+    Tl = b - a
+    B, H, D = cfg.batch, cfg.kv_heads, cfg.head_dim
+    s_c = case["channel_scale"]
+    gk = torch.Generator(device=dev).manual_seed(seed + 100)
+    gv = torch.Generator(device=dev).manual_seed(seed + 103)
+    idx = torch.empty(B, H, Tl, cfg.n_blocks, dtype=torch.uint8, device=dev)
+    heavy = None
+    if cfg.n_heavy:
+        heavy = torch.empty(B, H, Tl, cfg.n_heavy, cfg.block_dim, dtype=torch.bfloat16, device=dev)
+    value = torch.empty(B, H, Tl, D, dtype=cfg.torch_dtype, device=dev)
+    heavy_dims = case["heavy_mask"].repeat_interleave(cfg.block_dim)[case["inv_perm"]]
+    for bb in range(B):
+        keys = torch.randn(H, cfg.seq_len, D, generator=gk, device=dev)[:, a:b] * s_c
+        if cfg.n_heavy:
+            keys[..., heavy_dims] = keys[..., heavy_dims].to(torch.bfloat16).float()
+        i, hv = codec.quantize_packed(keys.to(cfg.torch_dtype if cfg.n_heavy else torch.float32), kv_heads=H)
+        idx[bb] = i
+        if heavy is not None:
+            heavy[bb] = hv
+        value[bb] = torch.randn(H, cfg.seq_len, D, generator=gv, device=dev)[:, a:b].to(cfg.torch_dtype)
+    query = case["query"].new_empty(B, cfg.q_heads, 1, D).copy_(
+        torch.randn(B, cfg.q_heads, 1, D, generator=torch.Generator(device=dev).manual_seed(seed + 4),
+                    device=dev).to(cfg.torch_dtype))
+    return codec, idx, heavy, value, query, case["scale"], Tl
+
+
+def algorithmic_bytes(cfg: DecodeConfig, local_tokens: int) -> int:
+    """Bytes one decode launch must move: per-token rows + codebooks + queries + outputs."""
+    vb = {"f32": 4, "bf16": 2, "f16": 2}[cfg.dtype]
+    per_token = cfg.bytes_per_kv_token()
+    consts = cfg.kv_heads * cfg.n_blocks * cfg.n_centroids * cfg.block_dim * 4 \
+        + 2 * cfg.batch * cfg.q_heads * cfg.head_dim * vb
+    return cfg.batch * cfg.kv_heads * local_tokens * per_token + consts
+
+
+# ----------------------------------------------------------------------------------- CPU baseline
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_reference_sample(cfg: DecodeConfig, budget_s: float = 12.0, seed: int = 0):
+    """Time the reference algorithm's CPU restatement on one (sequence, KV head) of the workload.
+
+    Returns (KV tokens/s, description).  Each repetition is exactly the reference's
+    per-(b, h) body of _apply_quantized_attention: dequantize, q @ k^T, softmax, P @ V.
+    """
+    from oracle import sunshape_oracle as O
+
+    T = cfg.seq_len
+    rng = np.random.default_rng(seed)
+    G, D, nb, bd, C = cfg.group, cfg.head_dim, cfg.n_blocks, cfg.block_dim, cfg.n_centroids
+    idx = rng.integers(0, C, size=(T, nb), dtype=np.uint8)
+    cents = rng.standard_normal((nb, C, bd), dtype=np.float32)
+    perm = rng.permutation(D)
+    inv = O.invert_permutation(perm)
+    hm = np.zeros(nb, dtype=bool)
+    pt = None
+    if cfg.n_heavy:
+        hm[:cfg.n_heavy] = True
+        pt = rng.standard_normal((T, nb, bd), dtype=np.float32)
+    q = O.bf16_round(rng.standard_normal((1, G, 1, D), dtype=np.float32))
+    v = O.bf16_round(rng.standard_normal((1, 1, T, D), dtype=np.float32))
+    heads = [(idx, hm if cfg.n_heavy else None, pt)]
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        O.apply_quantized_attention(q, heads, v, centroids_for_head=lambda h: cents, inv_perm=inv,
+                                    scale=1.0 / np.sqrt(D), query_dtype=cfg.dtype, value_dtype=cfg.dtype)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or reps >= 10000:
+            break
+    return reps * T / el, f"{reps} x one (sequence, KV head) of {T} tokens, G={G} (oracle port, numpy)"
+
+
+# ----------------------------------------------------------------------------------- timing
+def time_steps(fn, steps: int, warmup: int, stream: torch.cuda.Stream, extra_events=False):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
+def run_ours(args, cfg: DecodeConfig):
+    from sunshape_b200 import vllm_attn_backend as vab
+    from sunshape_b200.distributed import KVShardedDecode
+
+    world, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    codec, idx, heavy, value, query, scale, Tl = build_shard(cfg, rank, world, dev)
+    keys = vab.SunShapeQuantizedKeys((), cfg.batch, cfg.kv_heads, Tl, indices=idx, heavy=heavy,
+                                     passthrough_blocks=codec.mixed_high_precision_blocks if cfg.n_heavy else None,
+                                     head_dim=cfg.head_dim, block_dim=cfg.block_dim)
+    stream = torch.cuda.current_stream(dev)
+    sharded = KVShardedDecode(codec) if world > 1 else None
+    out = torch.empty(cfg.batch, cfg.q_heads, 1, cfg.head_dim, device=dev, dtype=value.dtype)
+
+    if world == 1:
+        def step():
+            vab._apply_quantized_attention(codec=codec, query=query, key=keys, value=value, attn_mask=None,
+                                           scale=scale, out=out)
+        launches_per_step = 1
+    else:
+        def step():
+            sharded(query, keys, value, scale=scale)
+        launches_per_step = 2
+
+    # decode kernel alone (events around the launch on its stream) for the roofline
+    def kernel_only():
+        if world == 1:
+            vab._apply_quantized_attention(codec=codec, query=query, key=keys, value=value, attn_mask=None,
+                                           scale=scale, out=out)
+        else:
+            sharded.partials(query, keys, value, scale=scale)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    kernel_ms = time_steps(kernel_only, max(20, args.steps // 4), 3, stream) / max(20, args.steps // 4)
+
+    sampler = ClockSampler(local)
+    barrier()
+    sampler.start()
+    time.sleep(0.3)           # let the sampler attach before the timed region
+    barrier()
+    t_ms = time_steps(step, args.steps, 0, stream)
+    barrier()
+    # e2e through the public API: pinned host query in, host output out, every step
+    from sunshape_b200.integration.vllm import SunShapeVLLMRuntimeState
+    from sunshape_b200.hf import SunShapeBundle
+    bundle = SunShapeBundle("synthetic", [0], 1.0, cfg.block_dim, "sunshape_base", 0, 0, 0, {0: codec}, {})
+    state = SunShapeVLLMRuntimeState("<memory>", "synthetic", "sunshape_base", 1.0, cfg.block_dim, [0], bundle,
+                                     str(dev))
+    impl = vab.SunShapeAttentionImpl(layer_idx=0, runtime_state=state)
+    q_host = query.cpu().pin_memory()
+    o_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        q = q_host.to(dev, non_blocking=True)
+        if world == 1:
+            o = impl.forward(q, keys, value, scale=scale)
+        else:
+            o = sharded(q, keys, value, scale=scale)
+        o_host.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e2e_ms = time_steps(e2e_step, args.steps, 0, stream)
+    barrier()
+    clocks = sampler.stop()
+
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([t_ms, e2e_ms, kernel_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms, e2e_ms, kernel_ms = t.tolist()
+
+    total_tokens = cfg.kv_tokens()
+    ms_per_step = t_ms / args.steps
+    value_tps = total_tokens / (ms_per_step * 1e-3)
+    e2e_tps = total_tokens / (e2e_ms / args.steps * 1e-3)
+    peak, peak_kind = measured_peaks()
+    alg = algorithmic_bytes(cfg, Tl)
+    achieved = alg / (kernel_ms * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", f"decode_kernel_{cfg.name}.json")
+    if os.path.exists(tp) and world == 1:
+        with open(tp) as f:
+            traffic = json.load(f).get("traffic_bytes_per_launch")
+    res = {
+        "metric": METRIC, "value": value_tps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded anisotropic log-normal keys, N(0,1) bf16 "
+                                                       "values/queries; no dataset)",
+        "config": {"workload": f"{cfg.name}: batch {cfg.batch}, {cfg.q_heads}/{cfg.kv_heads} heads, head_dim "
+                               f"{cfg.head_dim}, context {cfg.seq_len}, block_dim {cfg.block_dim}, "
+                               f"{cfg.n_centroids} codewords, {cfg.n_heavy} heavy blocks",
+                   "global_batch": cfg.batch, "seq_len": cfg.seq_len, "parallelism": f"kv-seq-split{world}",
+                   "kv_tokens_per_step": total_tokens, "bytes_per_kv_token": cfg.bytes_per_kv_token(),
+                   "l2": "inputs larger than L2 (no flush needed)"},
+        "hbm_gbs": achieved, "query_scores_per_s": value_tps * cfg.group,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "decode_kernel", "kernel_ms": kernel_ms, "algorithmic_bytes_per_launch": alg,
+                     "frac_of_nominal_8tbs": achieved / 8000.0},
+        "e2e": {"value": e2e_tps, "unit": UNIT, "h2d_bytes_per_step": query.numel() * query.element_size(),
+                "d2h_bytes_per_step": out.numel() * out.element_size()},
+        "clocks": clocks,
+        "gpu_launches": args.steps * launches_per_step,
+    }
+    return res, rank, world
+
+
+def run_extra_configs(args):
+    """N=1 figures for the other decode configs and the c3 encode path (parity configs; informational)."""
+    from sunshape_b200 import vllm_attn_backend as vab
+
+    dev = torch.device("cuda", 0)
+    peak, _ = measured_peaks()
+    extra = {}
+    for name in ("c2", "c3", "c4"):
+        cfg = CONFIGS[name]
+        codec, idx, heavy, value, query, scale, Tl = build_shard(cfg, 0, 1, dev)
+        keys = vab.SunShapeQuantizedKeys((), cfg.batch, cfg.kv_heads, Tl, indices=idx, heavy=heavy,
+                                         passthrough_blocks=codec.mixed_high_precision_blocks if cfg.n_heavy else None)
+        out = torch.empty(cfg.batch, cfg.q_heads, 1, cfg.head_dim, device=dev, dtype=value.dtype)
+
+        def step():
+            vab._apply_quantized_attention(codec=codec, query=query, key=keys, value=value, attn_mask=None,
+                                           scale=scale, out=out)
+        n = 100
+        ms = time_steps(step, n, 5, torch.cuda.current_stream(dev)) / n
+        alg = algorithmic_bytes(cfg, Tl)
+        extra[name] = {"kv_tokens_per_s": cfg.kv_tokens() / (ms * 1e-3), "ms_per_step": ms,
+                       "hbm_gbs": alg / (ms * 1e-3) / 1e9, "frac": alg / (ms * 1e-3) / 1e9 / peak}
+        if name == "c3":
+            # encode: append 16384 fp32 keys per (sequence, KV head)
+            kk = torch.randn(cfg.batch, cfg.kv_heads, cfg.seq_len, cfg.head_dim, device=dev)
+            ms_e = time_steps(lambda: codec.quantize_packed(kk, kv_heads=cfg.kv_heads), 5, 2,
+                              torch.cuda.current_stream(dev)) / 5
+            nkeys = kk.shape[0] * kk.shape[1] * kk.shape[2]
+            byt = nkeys * (cfg.head_dim * 4 + cfg.n_blocks)
+            extra["c3_encode"] = {"keys_per_s": nkeys / (ms_e * 1e-3), "ms": ms_e, "hbm_gbs": byt / (ms_e * 1e-3) / 1e9,
+                                  "argmin_compares_per_s": nkeys * cfg.n_blocks * cfg.n_centroids / (ms_e * 1e-3)}
+            del kk
+        del codec, idx, heavy, value, query, keys, out
+        torch.cuda.empty_cache()
+    return extra
+
+
+def run_reference(args, cfg: DecodeConfig):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    per_step = []
+    desc = ""
+    for _ in range(args.warmup):
+        cpu_reference_sample(cfg, budget_s=1.0)
+    for _ in range(args.steps):
+        tps, desc = cpu_reference_sample(cfg, budget_s=max(1.0, 60.0 / max(args.steps, 1)))
+        per_step.append(tps)
+    v = statistics.median(per_step)
+    cores = cpu_threads()
+    return {
+        "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": cfg.kv_tokens() / v * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": cfg.name, "global_batch": cfg.batch, "seq_len": cfg.seq_len,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="c5", choices=sorted(CONFIGS))
+    ap.add_argument("--no-extra", action="store_true", help="skip the N=1 figures for the other configs")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.workload]
+
+    if args.impl == "reference":
+        res = run_reference(args, cfg)
+        if res is not None:
+            print(json.dumps(res))
+        return
+
+    res, rank, world = run_ours(args, cfg)
+    if world == 1:
+        if not args.no_cpu:
+            tps, desc = cpu_reference_sample(cfg, budget_s=12.0)
+            res["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                                   "sample": desc}
+        if not args.no_extra:
+            res["other_configs_n1"] = run_extra_configs(args)
+    if rank == 0:
+        print(json.dumps(res))
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,422 @@
+// extern "C" boundary of libsunshape_b200.so: argument validation with
+// reference-style reason strings, template dispatch and launch configuration.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "decode.cuh"
+#include "encode.cuh"
+
+namespace sunshape {
+// Cross-shard merge of (m, l, acc) partial sets: one CTA per row.
+__global__ void merge_partials_kernel(const float* __restrict__ parts, int n_parts, int64_t rows, int dv,
+                                      void* out, int out_dtype) {
+  const int64_t r = blockIdx.x;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  for (int d = threadIdx.x; d < dv; d += blockDim.x) {
+    float M = NEG_INF;
+    for (int k = 0; k < n_parts; ++k) M = fmaxf(M, parts[(k * rows + r) * (dv + 2)]);
+    float Lsum = 0.f, A = 0.f;
+    if (M != NEG_INF) {
+      for (int k = 0; k < n_parts; ++k) {
+        const float* src = parts + (k * rows + r) * (dv + 2);
+        if (src[0] == NEG_INF) continue;
+        const float sc = fast_exp2((src[0] - M) * kLog2e);
+        Lsum = fmaf(src[1], sc, Lsum);
+        A = fmaf(src[2 + d], sc, A);
+      }
+    }
+    store_from_float(out, r * dv + d, out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
+  }
+}
+
+}  // namespace sunshape
+
+using namespace sunshape;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(SUNSHAPE_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return SUNSHAPE_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int dtype_size(int dt) {
+  switch (dt) {
+    case SUNSHAPE_F32: case SUNSHAPE_I32: return 4;
+    case SUNSHAPE_BF16: case SUNSHAPE_F16: case SUNSHAPE_I16: return 2;
+    case SUNSHAPE_U8: return 1;
+    default: return 0;
+  }
+}
+
+bool is_float_dtype(int dt) { return dt == SUNSHAPE_F32 || dt == SUNSHAPE_BF16 || dt == SUNSHAPE_F16; }
+
+int check_codec(const sunshape_codec_t* c) {
+  if (!c) return fail(SUNSHAPE_E_INVALID, "codec descriptor is NULL.");
+  if (!c->centroids || !c->permutation) return fail(SUNSHAPE_E_INVALID, "codec centroids / permutation pointer is NULL.");
+  if (c->block_dim <= 0 || c->head_dim <= 0 || c->head_dim % c->block_dim != 0)
+    return fail(SUNSHAPE_E_INVALID, "head_dim must be divisible by block_dim");
+  if (c->n_centroids <= 0) return fail(SUNSHAPE_E_INVALID, "n_centroids must be positive.");
+  if (c->n_cb <= 0) return fail(SUNSHAPE_E_INVALID, "n_cb (number of codebooks) must be positive.");
+  if (c->head_dim > 256) return fail(SUNSHAPE_E_UNSUPPORTED, "head_dim > 256 is not supported by the B200 kernels.");
+  if (c->n_heavy < 0 || c->n_heavy > c->head_dim / c->block_dim || (c->n_heavy > 0 && !c->heavy_mask))
+    return fail(SUNSHAPE_E_INVALID, "n_heavy must count the nonzero heavy_mask entries.");
+  return SUNSHAPE_OK;
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+struct DecodePlan {
+  int gp = 0;           // padded rows per launch (4, 8 or 16)
+  int chunk_rows = 0;   // rows per launch
+  int stages = 0;
+  int smem = 0;
+  DecodeParams prm{};
+  int64_t grid = 0;
+  int64_t ws_bytes = 0;
+};
+
+int pick_gp(int rows) { return rows <= 4 ? 4 : (rows <= 8 ? 8 : 16); }
+
+// Lay out shared memory and the split for one launch configuration.
+// Returns false if it cannot fit.
+bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_heavy_max, int bd,
+                 int hsize, bool scores_only, int n_heads, int T, int rows, std::string& why) {
+  int gp = pick_gp(rows);
+  const int nbh = (nb + 7) / 8;
+  if (nbh > 4) {
+    why = "n_blocks > 32 is not supported by the fused LUT kernel (LUT would not fit in shared memory).";
+    return false;
+  }
+  for (;;) {
+    const int lut_bytes = nbh * 8 * C * gp * 4;
+    const int stg_bytes = scores_only ? 0 : kWarps * gp * (dv + 2) * 4;
+    const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
+    const int off_perm = 256;
+    const int off_hslot = off_perm + round_up(D * 4, 16);
+    const int off_q = round_up(off_hslot + 64, 16);
+    const int off_p = round_up(off_q + gp * D * 4, 16);
+    const int off_lut = round_up(off_p + kWarps * (kWarpTokens + 1) * gp * 4, 128);
+    const int off_stage = off_lut + region;
+    const int vpart = scores_only ? 0 : round_up(kTileTokens * dv * vsize, 128);
+    const int ipart = round_up(kTileTokens * nb + 32, 128);
+    const int hpart = n_heavy_max > 0 ? round_up(kTileTokens * n_heavy_max * bd * hsize + 32, 128) : 0;
+    const int stage_bytes = vpart + ipart + hpart;
+    const int stages = std::min(kMaxStages, (kSmemLimit - off_stage) / stage_bytes);
+    const bool regs_ok = scores_only || gp * (dv / 32) <= 64;
+    if (stages >= 2 && regs_ok) {
+      pl.gp = gp;
+      pl.chunk_rows = std::min(rows, gp);
+      pl.stages = stages;
+      pl.smem = off_stage + stages * stage_bytes;
+      DecodeParams& p = pl.prm;
+      p.stages = stages;
+      p.stage_bytes = stage_bytes;
+      p.off_stage_idx = vpart;
+      p.off_stage_heavy = vpart + ipart;
+      p.off_perm = off_perm;
+      p.off_hslot = off_hslot;
+      p.off_q = off_q;
+      p.off_p = off_p;
+      p.off_lut = off_lut;
+      p.off_stage = off_stage;
+      const int tph = (T + kTileTokens - 1) / kTileTokens;
+      const int64_t total = (int64_t)n_heads * tph;
+      pl.grid = std::min<int64_t>(num_sms(), total);
+      const int64_t per_cta = (total + pl.grid - 1) / pl.grid;
+      p.tph = tph;
+      p.total_tiles = total;
+      p.max_seg = (int)((per_cta + tph - 1) / tph + 1);
+      const int64_t slots = pl.grid * p.max_seg * gp * (int64_t)(dv + 2) * 4;
+      pl.ws_bytes = 256 + round_up(n_heads * 4, 256) + slots;
+      return true;
+    }
+    if (gp == 4) break;
+    gp /= 2;
+  }
+  why = "decode configuration does not fit in shared memory / registers (n_blocks, n_centroids, rows).";
+  return false;
+}
+
+template <int GP, int DV, typename VT, bool SO>
+void run(const DecodePlan& pl, cudaStream_t st) {
+  DecodeLaunch l{pl.prm, pl.smem, pl.grid};
+  launch_decode_t<GP, DV, VT, SO>(l, st);
+}
+
+template <int GP, bool SO>
+int launch_decode_dv(const DecodePlan& pl, int dv, int vdt, cudaStream_t st) {
+  if constexpr (SO) {
+    run<GP, 64, float, true>(pl, st);
+    return SUNSHAPE_OK;
+  } else {
+#define SUNSHAPE_DV_CASE(DVV)                                                      \
+  if constexpr (GP * DVV / 32 <= 64) {                                             \
+    if (dv == DVV) {                                                               \
+      if (vdt == SUNSHAPE_F32) run<GP, DVV, float, false>(pl, st);                 \
+      else if (vdt == SUNSHAPE_BF16) run<GP, DVV, __nv_bfloat16, false>(pl, st);   \
+      else run<GP, DVV, __half, false>(pl, st);                                    \
+      return SUNSHAPE_OK;                                                          \
+    }                                                                              \
+  }
+  SUNSHAPE_DV_CASE(64)
+  SUNSHAPE_DV_CASE(128)
+  SUNSHAPE_DV_CASE(256)
+#undef SUNSHAPE_DV_CASE
+  }
+  return fail(SUNSHAPE_E_UNSUPPORTED, "value_dim must be 64, 128 or 256 for the fused decode kernel.");
+}
+
+template <bool SO>
+int launch_decode(const DecodePlan& pl, int dv, int vdt, cudaStream_t st) {
+  switch (pl.gp) {
+    case 4: return launch_decode_dv<4, SO>(pl, dv, vdt, st);
+    case 8: return launch_decode_dv<8, SO>(pl, dv, vdt, st);
+    default: return launch_decode_dv<16, SO>(pl, dv, vdt, st);
+  }
+}
+
+int check_kv(const sunshape_kv_t* kv, const sunshape_codec_t* c, bool need_value) {
+  if (!kv) return fail(SUNSHAPE_E_INVALID, "KV descriptor is NULL.");
+  if (!kv->indices) return fail(SUNSHAPE_E_INVALID, "Quantized key must expose an indices buffer.");
+  if (kv->seq_len < 0) return fail(SUNSHAPE_E_INVALID, "seq_len must be >= 0.");
+  if (kv->head_stride < kv->seq_len) return fail(SUNSHAPE_E_INVALID, "head_stride must be >= seq_len.");
+  if (need_value) {
+    if (!kv->value) return fail(SUNSHAPE_E_INVALID, "value buffer is NULL.");
+    if (!is_float_dtype(kv->value_dtype)) return fail(SUNSHAPE_E_INVALID, "value dtype must be F32, BF16 or F16.");
+    if (!aligned16(kv->value)) return fail(SUNSHAPE_E_INVALID, "value buffer must be 16-byte aligned.");
+  }
+  if (!aligned16(kv->indices)) return fail(SUNSHAPE_E_INVALID, "indices buffer must be 16-byte aligned.");
+  if (c->heavy_mask && kv->heavy) {
+    if (kv->heavy_dtype != SUNSHAPE_BF16 && kv->heavy_dtype != SUNSHAPE_F32)
+      return fail(SUNSHAPE_E_INVALID, "heavy (passthrough) dtype must be BF16 or F32.");
+    if (!aligned16(kv->heavy)) return fail(SUNSHAPE_E_INVALID, "heavy buffer must be 16-byte aligned.");
+  }
+  return SUNSHAPE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int sunshape_abi_version(void) { return SUNSHAPE_ABI_VERSION; }
+
+const char* sunshape_last_error(void) { return g_last_error.c_str(); }
+
+int sunshape_encode(const sunshape_codec_t* codec, const void* keys, int32_t keys_dtype, int32_t n_heads,
+                    int32_t kv_heads, int32_t n_tokens, int64_t key_head_stride, int64_t key_token_stride,
+                    void* indices_out, int32_t index_dtype, void* heavy_out, int32_t heavy_dtype,
+                    int64_t out_head_stride, void* stream) {
+  if (int rc = check_codec(codec)) return rc;
+  if (!keys || !indices_out) return fail(SUNSHAPE_E_INVALID, "keys / indices_out pointer is NULL.");
+  if (!is_float_dtype(keys_dtype)) return fail(SUNSHAPE_E_INVALID, "keys dtype must be F32, BF16 or F16.");
+  if (index_dtype != SUNSHAPE_U8 && index_dtype != SUNSHAPE_I16 && index_dtype != SUNSHAPE_I32)
+    return fail(SUNSHAPE_E_INVALID, "index dtype must be U8, I16 or I32.");
+  const int C = codec->n_centroids;
+  if ((index_dtype == SUNSHAPE_U8 && C > 256) || (index_dtype == SUNSHAPE_I16 && C > 65535))
+    return fail(SUNSHAPE_E_INVALID, "index dtype is too narrow for n_centroids (codec.py:78-83 rule).");
+  if (n_heads < 0 || n_tokens < 0 || kv_heads <= 0) return fail(SUNSHAPE_E_INVALID, "negative size.");
+  if (out_head_stride < n_tokens) return fail(SUNSHAPE_E_INVALID, "out_head_stride must be >= n_tokens.");
+  if (codec->heavy_mask && !heavy_out)
+    return fail(SUNSHAPE_E_INVALID, "heavy_out is required when the codec has a heavy-block mask.");
+  if (heavy_out && heavy_dtype != SUNSHAPE_BF16 && heavy_dtype != SUNSHAPE_F32)
+    return fail(SUNSHAPE_E_INVALID, "heavy dtype must be BF16 or F32.");
+  if (n_heads == 0 || n_tokens == 0) return SUNSHAPE_OK;
+  const int D = codec->head_dim, bd = codec->block_dim;
+  EncodeParams p{};
+  p.keys = keys; p.keys_dtype = keys_dtype; p.key_hs = key_head_stride; p.key_ts = key_token_stride;
+  p.n_tokens = n_tokens; p.kv_heads = kv_heads;
+  p.cb = codec->centroids; p.n_cb = codec->n_cb; p.perm = codec->permutation; p.heavy_mask = codec->heavy_mask;
+  p.nb = D / bd; p.bd = bd; p.C = C; p.D = D;
+  p.idx_out = indices_out; p.index_dtype = index_dtype; p.heavy_out = heavy_out; p.heavy_dtype = heavy_dtype;
+  p.out_hs = out_head_stride;
+  const int smem = (kEncRows * (D + 1) + C * bd + C + D) * 4 + 64;
+  if (smem > kSmemLimit) return fail(SUNSHAPE_E_UNSUPPORTED, "encode: codebook too large for shared memory.");
+  dim3 grid((n_tokens + kEncRows - 1) / kEncRows, n_heads);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define SUNSHAPE_ENC_CASE(B)                                                         \
+  case B: {                                                                          \
+    cudaFuncSetAttribute(encode_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+    encode_kernel<B><<<grid, kEncRows, smem, st>>>(p);                               \
+    break;                                                                           \
+  }
+  switch (bd) {
+    SUNSHAPE_ENC_CASE(1)
+    SUNSHAPE_ENC_CASE(2)
+    SUNSHAPE_ENC_CASE(4)
+    SUNSHAPE_ENC_CASE(8)
+    SUNSHAPE_ENC_CASE(16)
+    default: return fail(SUNSHAPE_E_UNSUPPORTED, "encode supports block_dim 1, 2, 4, 8 or 16.");
+  }
+#undef SUNSHAPE_ENC_CASE
+  return cuda_status("encode launch");
+}
+
+int sunshape_dequantize(const sunshape_codec_t* codec, const sunshape_kv_t* kv, int32_t n_heads, int32_t kv_heads,
+                        float* out, void* stream) {
+  if (int rc = check_codec(codec)) return rc;
+  if (int rc = check_kv(kv, codec, false)) return rc;
+  if (!out) return fail(SUNSHAPE_E_INVALID, "out pointer is NULL.");
+  if (codec->heavy_mask && !kv->heavy)
+    return fail(SUNSHAPE_E_INVALID, "Mixed-precision quantized keys are missing passthrough values.");
+  if (n_heads == 0 || kv->seq_len == 0) return SUNSHAPE_OK;
+  DequantParams p{};
+  p.idx = kv->indices; p.index_dtype = kv->index_dtype; p.heavy = kv->heavy; p.heavy_dtype = kv->heavy_dtype;
+  p.head_stride = kv->head_stride; p.T = kv->seq_len; p.kv_heads = kv_heads;
+  p.cb = codec->centroids; p.n_cb = codec->n_cb; p.perm = codec->permutation; p.heavy_mask = codec->heavy_mask;
+  p.D = codec->head_dim; p.bd = codec->block_dim; p.nb = p.D / p.bd; p.C = codec->n_centroids; p.out = out;
+  const int64_t n = (int64_t)kv->seq_len * p.D;
+  dim3 grid((unsigned)std::min<int64_t>((n + 255) / 256, 4096), n_heads);
+  dequant_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_status("dequantize launch");
+}
+
+static int fill_common(DecodeParams& p, const sunshape_codec_t* codec, const sunshape_kv_t* kv, int n_heads,
+                       int kv_heads) {
+  p.cb = codec->centroids; p.n_cb = codec->n_cb; p.perm = codec->permutation; p.heavy_mask = codec->heavy_mask;
+  p.D = codec->head_dim; p.bd = codec->block_dim; p.nb = p.D / p.bd; p.C = codec->n_centroids;
+  p.nbh = (p.nb + 7) / 8;
+  p.idx = reinterpret_cast<const uint8_t*>(kv->indices);
+  p.heavy = kv->heavy; p.heavy_dtype = kv->heavy ? kv->heavy_dtype : SUNSHAPE_BF16;
+  p.v = kv->value; p.T = kv->seq_len; p.head_stride = kv->head_stride; p.n_heads = n_heads;
+  p.kv_heads = kv_heads;
+  return SUNSHAPE_OK;
+}
+
+static int check_decode_codec(const sunshape_codec_t* codec, const sunshape_kv_t* kv) {
+  if (kv->index_dtype != SUNSHAPE_U8)
+    return fail(SUNSHAPE_E_UNSUPPORTED, "the fused LUT kernels need uint8 indices (n_centroids <= 256).");
+  if (codec->n_centroids > 256) return fail(SUNSHAPE_E_UNSUPPORTED, "n_centroids > 256 is not supported by the LUT kernels.");
+  if (codec->heavy_mask && !kv->heavy)
+    return fail(SUNSHAPE_E_INVALID, "Mixed-precision quantized keys are missing passthrough values.");
+  return SUNSHAPE_OK;
+}
+
+int sunshape_attention_scores(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
+                              int32_t query_dtype, int32_t n_heads, int32_t kv_heads, int32_t rows, float scale,
+                              float* scores_out, void* stream) {
+  if (int rc = check_codec(codec)) return rc;
+  if (int rc = check_kv(kv, codec, false)) return rc;
+  if (int rc = check_decode_codec(codec, kv)) return rc;
+  if (!query || !scores_out) return fail(SUNSHAPE_E_INVALID, "query / scores_out pointer is NULL.");
+  if (!is_float_dtype(query_dtype)) return fail(SUNSHAPE_E_INVALID, "query dtype must be F32, BF16 or F16.");
+  if (rows <= 0 || rows > 16) return fail(SUNSHAPE_E_UNSUPPORTED, "scores: rows per head must be in [1, 16].");
+  if (n_heads == 0 || kv->seq_len == 0) return SUNSHAPE_OK;
+  DecodePlan pl;
+  std::string why;
+  const int nb = codec->head_dim / codec->block_dim;
+  const int hsz = kv->heavy_dtype == SUNSHAPE_F32 ? 4 : 2;
+  if (!plan_decode(pl, nb, codec->n_centroids, codec->head_dim, 64, 2, codec->heavy_mask ? codec->n_heavy : 0,
+                   codec->block_dim, hsz, true, n_heads, kv->seq_len, rows, why))
+    return fail(SUNSHAPE_E_UNSUPPORTED, why);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int r0 = 0; r0 < rows; r0 += pl.chunk_rows) {
+    DecodeParams p = pl.prm;
+    fill_common(p, codec, kv, n_heads, kv_heads);
+    p.q = query; p.q_dtype = query_dtype; p.R = rows; p.r0 = r0; p.Rc = std::min(pl.chunk_rows, rows - r0);
+    p.L = 1; p.G = rows; p.q_heads = kv_heads * rows;
+    p.scale = scale; p.has_scale = std::isnan(scale) ? 0 : 1;
+    p.scores_out = scores_out;
+    DecodePlan pc = pl;
+    pc.prm = p;
+    if (int rc = launch_decode<true>(pc, 64, SUNSHAPE_F32, st)) return rc;
+  }
+  return cuda_status("scores launch");
+}
+
+int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_t rows, int32_t value_dim) {
+  if (n_heads <= 0 || seq_len <= 0 || rows <= 0) return 256;
+  // the slot area depends only on the grid, the split and (gp, value_dim): use the largest gp
+  const int gp = pick_gp(rows);
+  const int tph = (seq_len + kTileTokens - 1) / kTileTokens;
+  const int64_t total = (int64_t)n_heads * tph;
+  const int64_t grid = std::min<int64_t>(num_sms(), total);
+  const int64_t per_cta = (total + grid - 1) / grid;
+  const int64_t max_seg = (per_cta + tph - 1) / tph + 1;
+  return 256 + round_up(n_heads * 4, 256) + grid * max_seg * gp * (int64_t)(value_dim + 2) * 4;
+}
+
+int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
+                              int32_t query_dtype, int32_t batch, int32_t q_heads, int32_t kv_heads,
+                              int32_t query_len, const void* mask, int32_t mask_dtype, int64_t mask_sb,
+                              int64_t mask_sh, int64_t mask_sq, float scale, void* out, int32_t out_dtype,
+                              float* partials, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (int rc = check_codec(codec)) return rc;
+  if (int rc = check_kv(kv, codec, true)) return rc;
+  if (int rc = check_decode_codec(codec, kv)) return rc;
+  if (!query) return fail(SUNSHAPE_E_INVALID, "query pointer is NULL.");
+  if (!is_float_dtype(query_dtype)) return fail(SUNSHAPE_E_INVALID, "query dtype must be F32, BF16 or F16.");
+  if (batch < 0 || q_heads <= 0 || kv_heads <= 0 || query_len <= 0)
+    return fail(SUNSHAPE_E_INVALID, "batch / heads / query_len must be positive.");
+  if (q_heads % kv_heads != 0) return fail(SUNSHAPE_E_INVALID, "Query head count must be divisible by kv-head count.");
+  if (!out && !partials) return fail(SUNSHAPE_E_INVALID, "one of out / partials must be given.");
+  if (out && !is_float_dtype(out_dtype)) return fail(SUNSHAPE_E_INVALID, "out dtype must be F32, BF16 or F16.");
+  if (mask && !is_float_dtype(mask_dtype)) return fail(SUNSHAPE_E_INVALID, "mask dtype must be F32, BF16 or F16.");
+  if (kv->seq_len == 0) return fail(SUNSHAPE_E_INVALID, "seq_len must be positive for decode attention.");
+  if (batch == 0) return SUNSHAPE_OK;
+  const int G = q_heads / kv_heads;
+  const int R = G * query_len;
+  const int n_heads = batch * kv_heads;
+  const int nb = codec->head_dim / codec->block_dim;
+  const int dv = kv->value_dim;
+  DecodePlan pl;
+  std::string why;
+  const int hsz = kv->heavy_dtype == SUNSHAPE_F32 ? 4 : 2;
+  if (!plan_decode(pl, nb, codec->n_centroids, codec->head_dim, dv, dtype_size(kv->value_dtype),
+                   codec->heavy_mask ? codec->n_heavy : 0, codec->block_dim, hsz, false, n_heads, kv->seq_len, R, why))
+    return fail(SUNSHAPE_E_UNSUPPORTED, why);
+  if (!workspace) return fail(SUNSHAPE_E_WORKSPACE, "decode workspace is NULL.");
+  if (workspace_bytes < pl.ws_bytes) return fail(SUNSHAPE_E_WORKSPACE, "decode workspace is too small.");
+  if (!aligned16(workspace)) return fail(SUNSHAPE_E_WORKSPACE, "decode workspace must be 16-byte aligned.");
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int r0 = 0; r0 < R; r0 += pl.chunk_rows) {
+    DecodeParams p = pl.prm;
+    fill_common(p, codec, kv, n_heads, kv_heads);
+    p.q = query; p.q_dtype = query_dtype; p.R = R; p.r0 = r0; p.Rc = std::min(pl.chunk_rows, R - r0);
+    p.L = query_len; p.G = G; p.q_heads = q_heads;
+    p.mask = mask; p.mask_dtype = mask_dtype; p.msb = mask_sb; p.msh = mask_sh; p.msq = mask_sq;
+    p.scale = scale; p.has_scale = std::isnan(scale) ? 0 : 1;
+    p.out = out; p.out_dtype = out_dtype; p.partials = partials;
+    p.err = reinterpret_cast<int*>(ws);
+    p.counters = reinterpret_cast<int*>(ws + 256);
+    p.slots = reinterpret_cast<float*>(ws + 256 + round_up(n_heads * 4, 256));
+    DecodePlan pc = pl;
+    pc.prm = p;
+    if (int rc = launch_decode<false>(pc, dv, kv->value_dtype, st)) return rc;
+  }
+  return cuda_status("decode launch");
+}
+
+int sunshape_merge_partials(const float* partials, int32_t n_parts, int64_t rows, int32_t value_dim, void* out,
+                            int32_t out_dtype, void* stream) {
+  if (!partials || !out) return fail(SUNSHAPE_E_INVALID, "partials / out pointer is NULL.");
+  if (n_parts <= 0 || rows < 0 || value_dim <= 0) return fail(SUNSHAPE_E_INVALID, "bad merge sizes.");
+  if (!is_float_dtype(out_dtype)) return fail(SUNSHAPE_E_INVALID, "out dtype must be F32, BF16 or F16.");
+  if (rows == 0) return SUNSHAPE_OK;
+  merge_partials_kernel<<<(unsigned)rows, std::min(256, round_up(value_dim, 32)), 0,
+                          reinterpret_cast<cudaStream_t>(stream)>>>(partials, n_parts, rows, value_dim, out,
+                                                                    out_dtype);
+  return cuda_status("merge launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,77 @@
+"""KV-sequence split of SunShape decode attention across GPUs (one process per GPU).
+
+The reference keeps the whole KV cache on one device and has no distributed code;
+long contexts here are sharded along the sequence: rank r owns tokens
+``[start_r, end_r)`` of every (sequence, KV head) -- indices, heavy blocks and
+values -- while codebooks, the permutation and the queries are replicated.  Each
+rank runs the fused decode kernel over its shard and emits unnormalised softmax
+partials ``(m, l, acc)`` per query row; ONE collective (an all-gather of the
+packed fp32 partials over NCCL / NVLink) brings every rank's partials to every
+rank, and a merge kernel combines them in a fixed rank order, so all ranks hold
+the identical final output:
+
+    M = max_r m_r,   L = sum_r l_r e^(m_r - M),   O = sum_r acc_r e^(m_r - M) / L.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .vllm_attn_backend import SunShapeQuantizedKeys, decode_partials
+
+
+def kv_shard_bounds(seq_len: int, world_size: int, rank: int) -> tuple[int, int]:
+    """Even contiguous split of ``seq_len`` tokens; the first ``seq_len % world_size`` ranks get one extra."""
+    if world_size <= 0 or not 0 <= rank < world_size:
+        raise ValueError("bad world_size / rank")
+    base, rem = divmod(int(seq_len), int(world_size))
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+def shard_mask(attn_mask: torch.Tensor | None, start: int, end: int) -> torch.Tensor | None:
+    return None if attn_mask is None else attn_mask[..., start:end]
+
+
+def gather_partials(partials: torch.Tensor, group=None) -> torch.Tensor:
+    """All-gather [rows, 2 + Dv] fp32 partials into [world, rows, 2 + Dv] (the only collective)."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world, *partials.shape), dtype=partials.dtype, device=partials.device)
+    dist.all_gather_into_tensor(out, partials.contiguous(), group=group)
+    return out
+
+
+def merge_gathered(gathered: torch.Tensor, out_shape, out_dtype) -> torch.Tensor:
+    """Merge [world, rows, 2 + Dv] partials on the GPU (fixed rank order)."""
+    Dv = gathered.shape[-1] - 2
+    out = torch.empty(gathered.shape[1], Dv, device=gathered.device, dtype=out_dtype)
+    _lib.merge_partials(gathered.contiguous(), out)
+    return out.view(*out_shape)
+
+
+class KVShardedDecode:
+    """Decode attention over a KV cache whose sequence is split across the ranks of ``group``."""
+
+    def __init__(self, codec, group=None):
+        self.codec = codec
+        self.group = group
+        self._partials = None
+
+    def partials(self, query, key: SunShapeQuantizedKeys, value, attn_mask=None, scale=None) -> torch.Tensor:
+        B, Hq, L, _ = query.shape
+        Dv = value.shape[-1]
+        shape = (B * Hq * L, 2 + Dv)
+        if self._partials is None or self._partials.shape != shape or self._partials.device != query.device:
+            self._partials = torch.empty(shape, device=query.device, dtype=torch.float32)
+        return decode_partials(codec=self.codec, query=query, key=key, value=value, attn_mask=attn_mask,
+                               scale=scale, partials=self._partials)
+
+    def forward(self, query, key: SunShapeQuantizedKeys, value, attn_mask=None, scale=None) -> torch.Tensor:
+        """Rank-local shard in, full merged output [B, Hq, L, Dv] (value dtype) out, on every rank."""
+        part = self.partials(query, key, value, attn_mask, scale)
+        gathered = gather_partials(part, self.group)
+        B, Hq, L, _ = query.shape
+        return merge_gathered(gathered, (B, Hq, L, value.shape[-1]), value.dtype)
+
+    __call__ = forward

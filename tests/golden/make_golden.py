@@ -1,0 +1,145 @@
+"""Generate golden vectors by running the REFERENCE SunShape code on seeded inputs.
+
+Run in a container that has the reference checkout (it is not needed anywhere else):
+
+    PYTHONPATH=<reference checkout> python tests/golden/make_golden.py
+
+For every case this imports the reference package unmodified, builds one codec
+per KV head by writing its buffers directly (the configs use per-KV-head
+codebooks; the reference keeps one codec per layer, so the oracle loops over
+heads), and records the reference's own outputs:
+
+* ``codec.quantize`` indices / passthrough      (codec.py:362-385)
+* ``_torch_attention_scores`` per head           (triton_kernels.py:300-311)
+* ``_apply_quantized_attention`` output          (vllm_attn_backend.py:216-253)
+
+The results are written to ``tests/golden/<case>.npz`` together with the inputs,
+so tests never need the reference at run time.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from sunshape_b200.workloads import CONFIGS, make_case  # noqa: E402
+
+CASES = {
+    # c1-shaped (fp32, GQA 7:1, D64, bd8) at T=1024
+    "g1_c1_fp32": dict(cfg=CONFIGS["c1"].with_(seq_len=1024), scale=None, mask=None),
+    # bf16 GQA 4:1, ragged T, 4-D additive mask with -inf holes, scale given
+    "g2_bf16_mask4d": dict(cfg=CONFIGS["c2"].with_(batch=2, q_heads=8, kv_heads=2, seq_len=333),
+                           scale="default", mask="4d"),
+    # SunShape-Mixed, 4 heavy blocks of 16
+    "g3_mixed": dict(cfg=CONFIGS["c4"].with_(batch=1, q_heads=8, kv_heads=2, seq_len=500),
+                     scale="default", mask=None),
+    # bd=4 (2 bits/dim, 32 blocks)
+    "g4_bd4": dict(cfg=CONFIGS["c3"].with_(batch=1, q_heads=4, kv_heads=1, seq_len=256),
+                   scale="default", mask="2d"),
+    # smallest: one token, MHA (G=1)
+    "g5_t1_g1": dict(cfg=CONFIGS["c1"].with_(q_heads=2, kv_heads=2, seq_len=1, dtype="bf16"),
+                     scale="default", mask=None),
+    # query_len 2 (non-causal) and a 3-D per-head mask, G=8
+    "g6_qlen2_mask3d": dict(cfg=CONFIGS["c5"].with_(batch=1, q_heads=16, kv_heads=2, seq_len=129,
+                                                    head_dim=64, query_len=2),
+                            scale="default", mask="3d"),
+}
+
+
+def _mask(kind, cfg, gen):
+    B, Hq, L, T = cfg.batch, cfg.q_heads, cfg.query_len, cfg.seq_len
+    if kind is None:
+        return None
+    if kind == "4d":
+        m = torch.randn(B, Hq, L, T, generator=gen) * 0.5
+        m[..., ::7] = float("-inf")
+        return m
+    if kind == "3d":
+        m = torch.randn(Hq, L, T, generator=gen)
+        m[:, :, -5:] = float("-inf")
+        return m
+    if kind == "2d":
+        m = torch.zeros(L, T)
+        m[:, : T // 3] = float("-inf")
+        return m
+    raise ValueError(kind)
+
+
+def run_case(name, spec):
+    from sunshape.codec import SunShapeBlockCodec
+    from sunshape.triton_kernels import _torch_attention_scores
+    from sunshape.vllm_attn_backend import SunShapeQuantizedKeys, _apply_quantized_attention
+
+    cfg = spec["cfg"]
+    case = make_case(cfg, device="cpu", seed=0)
+    scale = None if spec["scale"] is None else case["scale"]
+    mask = _mask(spec["mask"], cfg, torch.Generator().manual_seed(5))
+    B, Hq, Hkv, D, T = cfg.batch, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.seq_len
+    G = cfg.group
+    mode = "profileperm_mixed_precision" if cfg.n_heavy else "profileperm_baseline"
+
+    codecs = []
+    for h in range(Hkv):
+        codec = SunShapeBlockCodec(head_dim=D, block_dim=cfg.block_dim, n_centroids=cfg.n_centroids,
+                                   mode=mode, device=torch.device("cpu"))
+        codec.permutation.copy_(case["perm"])
+        codec.inv_permutation.copy_(case["inv_perm"])
+        codec.centroids.copy_(case["centroids"][h])
+        codec.mixed_high_precision_blocks.copy_(case["heavy_mask"])
+        codecs.append(codec)
+
+    nb, bd = cfg.n_blocks, cfg.block_dim
+    indices = np.zeros((B, Hkv, T, nb), dtype=np.uint8)
+    passthrough = np.zeros((B, Hkv, T, nb, bd), dtype=np.float32)
+    scores = np.zeros((B, Hkv, G * cfg.query_len, T), dtype=np.float32)
+    out = torch.empty(B, Hq, cfg.query_len, D, dtype=cfg.torch_dtype)
+    for b in range(B):
+        for h in range(Hkv):
+            qk = codecs[h].quantize(case["keys"][b, h])
+            indices[b, h] = qk.indices.numpy()
+            if qk.passthrough_values is not None:
+                passthrough[b, h] = qk.passthrough_values.numpy()
+            qs = case["query"][b, h * G:(h + 1) * G]
+            if scale is not None:
+                qs = qs * float(scale)
+            scores[b, h] = _torch_attention_scores(codecs[h], qs.reshape(-1, D), qk).numpy()
+            keys_obj = SunShapeQuantizedKeys(quantized_heads=(qk,), batch_size=1, num_kv_heads=1, seq_len=T)
+            m = None
+            if mask is not None:
+                if mask.ndim == 4:
+                    m = mask[b:b + 1, h * G:(h + 1) * G]
+                elif mask.ndim == 3:
+                    m = mask[h * G:(h + 1) * G]
+                else:
+                    m = mask
+            out[b:b + 1, h * G:(h + 1) * G] = _apply_quantized_attention(
+                codec=codecs[h], query=case["query"][b:b + 1, h * G:(h + 1) * G], key=keys_obj,
+                value=case["value"][b:b + 1, h:h + 1], attn_mask=m, scale=scale)
+
+    def f32(t):
+        return t.float().numpy()
+
+    payload = dict(
+        B=B, Hq=Hq, Hkv=Hkv, D=D, T=T, L=cfg.query_len, block_dim=bd, n_centroids=cfg.n_centroids,
+        dtype=cfg.dtype, scale=np.float64("nan") if scale is None else np.float64(scale),
+        keys=f32(case["keys"]), perm=case["perm"].numpy(), inv_perm=case["inv_perm"].numpy(),
+        centroids=f32(case["centroids"]), heavy_mask=case["heavy_mask"].numpy(),
+        query=f32(case["query"]), value=f32(case["value"]),
+        mask=np.zeros(0, np.float32) if mask is None else f32(mask),
+        ref_indices=indices, ref_passthrough=passthrough, ref_scores=scores, ref_out=f32(out),
+    )
+    path = os.path.join(HERE, f"{name}.npz")
+    np.savez_compressed(path, **payload)
+    print(f"{name}: wrote {os.path.getsize(path) / 1024:.0f} KiB")
+
+
+if __name__ == "__main__":
+    import sunshape  # noqa: F401  (must resolve to the reference checkout)
+    torch.manual_seed(0)
+    for n, s in CASES.items():
+        run_case(n, s)

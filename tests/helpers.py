@@ -1,0 +1,65 @@
+"""Shared test helpers: golden fixtures, codec construction and tolerance checks."""
+from __future__ import annotations
+
+import glob
+import os
+
+import numpy as np
+import torch
+
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+GOLDEN_CASES = sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+
+# tolerances stated by the north star: fp32 accumulation rel 1e-5, bf16 outputs 2e-2
+TOL_F32 = 1e-5
+TOL_BF16 = 2e-2
+
+
+def load_golden(name: str) -> dict:
+    z = np.load(os.path.join(GOLDEN_DIR, name + ".npz"))
+    g = {k: z[k] for k in z.files}
+    for k in ("B", "Hq", "Hkv", "D", "T", "L", "block_dim", "n_centroids"):
+        g[k] = int(g[k])
+    g["dtype"] = str(g["dtype"])
+    s = float(g["scale"])
+    g["scale"] = None if np.isnan(s) else s
+    g["mask"] = g["mask"] if g["mask"].size else None
+    return g
+
+
+def torch_dtype(name: str):
+    return {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[name]
+
+
+def make_codec(perm, centroids, heavy_mask, head_dim, block_dim, n_centroids, device):
+    """SunShapeBlockCodec with per-KV-head codebooks written directly (no fitting)."""
+    from sunshape_b200.codec import SunShapeBlockCodec
+
+    perm = torch.as_tensor(perm, dtype=torch.long)
+    cents = torch.as_tensor(centroids, dtype=torch.float32)
+    heavy = torch.as_tensor(heavy_mask, dtype=torch.bool)
+    mode = "profileperm_mixed_precision" if bool(heavy.any()) else "profileperm_baseline"
+    codec = SunShapeBlockCodec(head_dim=head_dim, block_dim=block_dim, n_centroids=n_centroids, mode=mode,
+                               device=torch.device(device), kv_heads=cents.shape[0] if cents.ndim == 4 else None)
+    codec.permutation.copy_(perm)
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(len(perm))
+    codec.inv_permutation.copy_(inv)
+    codec.centroids.copy_(cents)
+    codec.mixed_high_precision_blocks.copy_(heavy)
+    codec.invalidate()
+    return codec
+
+
+def assert_close_normwise(actual, expected, rtol, what=""):
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    assert a.shape == e.shape, (a.shape, e.shape)
+    nan_a, nan_e = np.isnan(a), np.isnan(e)
+    assert (nan_a == nan_e).all(), f"{what}: NaN pattern differs ({nan_a.sum()} vs {nan_e.sum()})"
+    fin = ~nan_e
+    if not fin.any():
+        return
+    scale = max(np.abs(e[fin]).max(), 1e-30)
+    err = np.abs(a[fin] - e[fin]).max()
+    assert err <= rtol * scale, f"{what}: max err {err:.3e} > {rtol:.1e} * {scale:.3e}"
