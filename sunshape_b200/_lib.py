@@ -125,6 +125,13 @@ def require_cuda(*tensors: torch.Tensor | None) -> torch.device:
     return dev
 
 
+def aligned16(t: torch.Tensor | None) -> torch.Tensor | None:
+    """Return t, or a fresh (16-byte aligned) contiguous copy if its data pointer is not 16-byte aligned."""
+    if t is None or t.data_ptr() % 16 == 0:
+        return t
+    return t.clone(memory_format=torch.contiguous_format)
+
+
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 

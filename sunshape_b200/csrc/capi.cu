@@ -5,7 +5,10 @@
 #include <cstring>
 #include <string>
 
+#include <cudaTypedefs.h>
+
 #include "decode.cuh"
+#include "decode_mma.cuh"
 #include "encode.cuh"
 
 namespace sunshape {
@@ -155,6 +158,114 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
   }
   why = "decode configuration does not fit in shared memory / registers (n_blocks, n_centroids, rows).";
   return false;
+}
+
+// Shared-memory carve-up and split for the tensor-core kernel (16-bit values).
+bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd, int hsize, int n_heads, int T,
+                     int rows, std::string& why) {
+  const int nbh = (nb + 7) / 8;
+  if (nbh > 4) {
+    why = "n_blocks > 32 is not supported by the fused LUT kernel (LUT would not fit in shared memory).";
+    return false;
+  }
+  if (dv != 64 && dv != 128 && dv != 256) {
+    why = "value_dim must be 64, 128 or 256 for the fused decode kernel.";
+    return false;
+  }
+  for (int gp = pick_gp(rows);; gp /= 2) {
+    const int nt = (gp + 7) / 8;
+    const int lut_bytes = nbh * 8 * kLutC * gp * 4;
+    const int stg_bytes = kWarpsM * gp * (dv + 2) * 4;
+    const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
+    const int off_perm = 256;
+    const int off_hslot = off_perm + round_up(D * 4, 16);
+    const int off_q = round_up(off_hslot + 64, 16);
+    const int off_p = round_up(off_q + gp * D * 4, 16);
+    const int off_lut = round_up(off_p + kWarpsM * (nt * 512 + 64), 128);
+    const int off_stage = round_up(off_lut + region, 1024);
+    const int vpart = (dv / 64) * kVBoxBytes;
+    const int ipart = round_up(kTileTokens * nb + 32, 128);
+    const int hpart = n_heavy > 0 ? round_up(kTileTokens * n_heavy * bd * hsize + 32, 128) : 0;
+    const int stage_bytes = round_up(vpart + ipart + hpart, 1024);
+    const int stages = std::min(kMaxStages, (kSmemLimit - 1024 - off_stage) / stage_bytes);
+    if (stages >= 2) {
+      pl.gp = gp;
+      pl.chunk_rows = std::min(rows, gp);
+      pl.stages = stages;
+      pl.smem = off_stage + stages * stage_bytes + 1024;
+      DecodeParams& p = pl.prm;
+      p.stages = stages;
+      p.stage_bytes = stage_bytes;
+      p.off_stage_idx = vpart;
+      p.off_stage_heavy = vpart + ipart;
+      p.off_perm = off_perm;
+      p.off_hslot = off_hslot;
+      p.off_q = off_q;
+      p.off_p = off_p;
+      p.off_lut = off_lut;
+      p.off_stage = off_stage;
+      const int tph = (T + kTileTokens - 1) / kTileTokens;
+      const int64_t total = (int64_t)n_heads * tph;
+      pl.grid = std::min<int64_t>(num_sms(), total);
+      const int64_t per_cta = (total + pl.grid - 1) / pl.grid;
+      p.tph = tph;
+      p.total_tiles = total;
+      p.max_seg = (int)((per_cta + tph - 1) / tph + 1);
+      pl.ws_bytes = 256 + round_up(n_heads * 4, 256) + pl.grid * p.max_seg * gp * (int64_t)(dv + 2) * 4;
+      return true;
+    }
+    if (gp == 4) break;
+  }
+  why = "decode configuration does not fit in shared memory (n_blocks, rows).";
+  return false;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q{};
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 2-D view [rows, dv] of the 16-bit values, boxes of 64 tokens x 64 columns, 128-byte swizzle.
+int make_value_map(CUtensorMap* map, const void* v, int dtype, int dv, int64_t rows) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(SUNSHAPE_E_CUDA, "cuTensorMapEncodeTiled is unavailable from the CUDA driver.");
+  const cuuint64_t dims[2] = {(cuuint64_t)dv, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)dv * 2};
+  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, dtype == SUNSHAPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(v), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SUNSHAPE_E_CUDA, "cuTensorMapEncodeTiled failed for the value tensor.");
+  return SUNSHAPE_OK;
+}
+
+template <int GP, int DV, typename VT>
+void run_mma(const DecodePlan& pl, cudaStream_t st) {
+  DecodeLaunch l{pl.prm, pl.smem, pl.grid};
+  launch_decode_mma_t<GP, DV, VT>(l, st);
+}
+
+int launch_decode_mma(const DecodePlan& pl, int dv, int vdt, cudaStream_t st) {
+#define SUNSHAPE_MMA_CASE(GPV, DVV)                                              \
+  if (pl.gp == GPV && dv == DVV) {                                              \
+    if (vdt == SUNSHAPE_BF16) run_mma<GPV, DVV, __nv_bfloat16>(pl, st);        \
+    else run_mma<GPV, DVV, __half>(pl, st);                                     \
+    return SUNSHAPE_OK;                                                          \
+  }
+  SUNSHAPE_MMA_CASE(4, 64) SUNSHAPE_MMA_CASE(4, 128) SUNSHAPE_MMA_CASE(4, 256)
+  SUNSHAPE_MMA_CASE(8, 64) SUNSHAPE_MMA_CASE(8, 128) SUNSHAPE_MMA_CASE(8, 256)
+  SUNSHAPE_MMA_CASE(16, 64) SUNSHAPE_MMA_CASE(16, 128) SUNSHAPE_MMA_CASE(16, 256)
+#undef SUNSHAPE_MMA_CASE
+  return fail(SUNSHAPE_E_UNSUPPORTED, "no tensor-core decode kernel for this (rows, value_dim).");
 }
 
 template <int GP, int DV, typename VT, bool SO>
@@ -381,9 +492,17 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
   DecodePlan pl;
   std::string why;
   const int hsz = kv->heavy_dtype == SUNSHAPE_F32 ? 4 : 2;
-  if (!plan_decode(pl, nb, codec->n_centroids, codec->head_dim, dv, dtype_size(kv->value_dtype),
-                   codec->heavy_mask ? codec->n_heavy : 0, codec->block_dim, hsz, false, n_heads, kv->seq_len, R, why))
-    return fail(SUNSHAPE_E_UNSUPPORTED, why);
+  const int n_heavy = codec->heavy_mask ? codec->n_heavy : 0;
+  const bool use_mma = kv->value_dtype != SUNSHAPE_F32;   // 16-bit values: tensor-core kernel
+  const bool ok = use_mma ? plan_decode_mma(pl, nb, codec->head_dim, dv, n_heavy, codec->block_dim, hsz, n_heads,
+                                            kv->seq_len, R, why)
+                          : plan_decode(pl, nb, codec->n_centroids, codec->head_dim, dv, dtype_size(kv->value_dtype),
+                                        n_heavy, codec->block_dim, hsz, false, n_heads, kv->seq_len, R, why);
+  if (!ok) return fail(SUNSHAPE_E_UNSUPPORTED, why);
+  if (use_mma) {
+    const int64_t rows_total = (int64_t)(n_heads - 1) * kv->head_stride + kv->seq_len;
+    if (int rc = make_value_map(&pl.prm.tmap_v, kv->value, kv->value_dtype, dv, rows_total)) return rc;
+  }
   if (!workspace) return fail(SUNSHAPE_E_WORKSPACE, "decode workspace is NULL.");
   if (workspace_bytes < pl.ws_bytes) return fail(SUNSHAPE_E_WORKSPACE, "decode workspace is too small.");
   if (!aligned16(workspace)) return fail(SUNSHAPE_E_WORKSPACE, "decode workspace must be 16-byte aligned.");
@@ -402,7 +521,9 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
     p.slots = reinterpret_cast<float*>(ws + 256 + round_up(n_heads * 4, 256));
     DecodePlan pc = pl;
     pc.prm = p;
-    if (int rc = launch_decode<false>(pc, dv, kv->value_dtype, st)) return rc;
+    if (int rc = use_mma ? launch_decode_mma(pc, dv, kv->value_dtype, st)
+                         : launch_decode<false>(pc, dv, kv->value_dtype, st))
+      return rc;
   }
   return cuda_status("decode launch");
 }

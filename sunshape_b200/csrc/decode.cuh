@@ -44,6 +44,8 @@ constexpr int kErrWaitFull = 101;
 constexpr int kErrWaitEmpty = 102;
 
 struct DecodeParams {
+  // value tiles for the tensor-core kernel: 2-D map over [rows, value_dim], box 64 x 64, 128B swizzle
+  CUtensorMap tmap_v;
   // query rows: row r of flat head hh lives at q + (hh * R + r) * D
   const void* q;
   int q_dtype;
@@ -193,12 +195,12 @@ __device__ __forceinline__ void load_value_row(const VT* src, float (&vf)[DPL]) 
 }
 
 // Build the LUT (and the permuted, scaled query rows) for flat head hh.
-template <int GP>
-__device__ void build_lut(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
-                          float* q_s, uint8_t* lut, int ctid) {
+template <int GP, int NTHREADS>
+__device__ void build_lut_t(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
+                            float* q_s, uint8_t* lut, int ctid) {
   constexpr int NH = GP / 4;
-  named_barrier(kBarConsumers, kConsumerThreads);
-  for (int e = ctid; e < GP * p.D; e += kConsumerThreads) {
+  named_barrier(kBarConsumers, NTHREADS);
+  for (int e = ctid; e < GP * p.D; e += NTHREADS) {
     const int g = e / p.D, dp = e - g * p.D;
     float v = 0.f;
     if (g < p.Rc) {
@@ -209,11 +211,11 @@ __device__ void build_lut(const DecodeParams& p, int64_t hh, const int* perm_s, 
     }
     q_s[g * p.D + dp] = v;
   }
-  named_barrier(kBarConsumers, kConsumerThreads);
+  named_barrier(kBarConsumers, NTHREADS);
   const int cbh = p.n_cb == 1 ? 0 : (int)((hh % p.kv_heads) % p.n_cb);
   const float* cb = p.cb + (int64_t)cbh * p.nb * p.C * p.bd;
   const int total = p.nbh * 8 * p.C;
-  for (int e = ctid; e < total; e += kConsumerThreads) {
+  for (int e = ctid; e < total; e += NTHREADS) {
     const int blo = e & 7, rest = e >> 3;
     const int k = rest / p.C, c = rest - k * p.C;
     const int b = blo + 8 * k;
@@ -235,7 +237,7 @@ __device__ void build_lut(const DecodeParams& p, int64_t hh, const int* perm_s, 
       *dst = make_float4(vals[4 * h], vals[4 * h + 1], vals[4 * h + 2], vals[4 * h + 3]);
     }
   }
-  named_barrier(kBarConsumers, kConsumerThreads);
+  named_barrier(kBarConsumers, NTHREADS);
 }
 
 // Producer warp: stream tiles [tb, te) into the stage ring.
@@ -288,6 +290,91 @@ __device__ void produce(const DecodeParams& p, int64_t tb, int64_t te, uint64_t*
       if (hbulk) bulk_g2s(st + p.off_stage_heavy, reinterpret_cast<const void*>(ha0), hbulk, &full[s]);
     }
     __syncwarp();
+  }
+}
+
+// End of a KV-head segment: `stg` holds NW per-warp partials [NW][GP][DV + 2] (m, l, acc).
+// Merge them; if this CTA is the head's only contributor write the result, else store
+// the CTA partial in the workspace slot and let the last contributor (atomic ticket)
+// merge all slots of the head.
+template <int GP, int DV, int NW>
+__device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t hh, int64_t tb, int64_t grid,
+                               int ctid, int* flag_s) {
+  constexpr int ROWF = DV + 2;
+  constexpr int NT = NW * 32;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const int64_t c_first = tile_owner(hh * p.tph, p.total_tiles, grid);
+  const int64_t c_last = tile_owner((hh + 1) * p.tph - 1, p.total_tiles, grid);
+  const bool sole = c_first == c_last;
+  const int seg_local = (int)(hh - tb / p.tph);
+  float* slot = p.slots + ((int64_t)blockIdx.x * p.max_seg + seg_local) * GP * ROWF;
+  for (int e = ctid; e < p.Rc * DV; e += NT) {
+    const int r = e / DV, d = e - r * DV;
+    float M = NEG_INF;
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, stg[(w * GP + r) * ROWF]);
+    float Lsum = 0.f, A = 0.f;
+    if (M != NEG_INF) {
+      for (int w = 0; w < NW; ++w) {
+        const float* src = stg + (w * GP + r) * ROWF;
+        const float sc = fast_exp2((src[0] - M) * kLog2e);
+        Lsum = fmaf(src[1], sc, Lsum);
+        A = fmaf(src[2 + d], sc, A);
+      }
+    }
+    if (sole) {
+      const int64_t orow = hh * p.R + p.r0 + r;
+      if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
+      if (p.partials) {
+        float* pr = p.partials + orow * (int64_t)(DV + 2);
+        pr[2 + d] = A;
+        if (d == 0) { pr[0] = M; pr[1] = Lsum; }
+      }
+    } else {
+      slot[r * ROWF + 2 + d] = A;
+      if (d == 0) { slot[r * ROWF] = M; slot[r * ROWF + 1] = Lsum; }
+    }
+  }
+  if (!sole) {
+    __threadfence();
+    named_barrier(kBarConsumers, NT);
+    if (ctid == 0) {
+      const int n_contrib = (int)(c_last - c_first + 1);
+      const int prev = atomicAdd(&p.counters[hh], 1);
+      flag_s[0] = prev == n_contrib - 1;
+    }
+    named_barrier(kBarConsumers, NT);
+    if (flag_s[0]) {
+      __threadfence();
+      for (int e = ctid; e < p.Rc * DV; e += NT) {
+        const int r = e / DV, d = e - r * DV;
+        float M = NEG_INF, Lsum = 0.f, A = 0.f;
+        for (int64_t c = c_first; c <= c_last; ++c) {
+          const int sl = (int)(hh - tile_start(c, p.total_tiles, grid) / p.tph);
+          const float* src = p.slots + ((c * p.max_seg + sl) * GP + r) * ROWF;
+          const float m = __ldcg(src);
+          if (m == NEG_INF) continue;
+          const float l = __ldcg(src + 1), a = __ldcg(src + 2 + d);
+          if (m > M) {
+            const float sc = fast_exp2((M - m) * kLog2e);
+            Lsum = Lsum * sc + l;
+            A = A * sc + a;
+            M = m;
+          } else {
+            const float sc = fast_exp2((m - M) * kLog2e);
+            Lsum = fmaf(l, sc, Lsum);
+            A = fmaf(a, sc, A);
+          }
+        }
+        const int64_t orow = hh * p.R + p.r0 + r;
+        if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
+        if (p.partials) {
+          float* pr = p.partials + orow * (int64_t)(DV + 2);
+          pr[2 + d] = A;
+          if (d == 0) { pr[0] = M; pr[1] = Lsum; }
+        }
+      }
+      if (ctid == 0) atomicExch(&p.counters[hh], 0);
+    }
   }
 }
 
@@ -355,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int64_t hh = f / p.tph;
     const int64_t fend = min(te, (hh + 1) * p.tph);
     const int i0 = (int)(f - tb), i1 = (int)(fend - tb);
-    build_lut<GP>(p, hh, perm_s, hslot_s, q_s, lut, ctid);
+    build_lut_t<GP, kConsumerThreads>(p, hh, perm_s, hslot_s, q_s, lut, ctid);
 
     float m_run[RPL], l_run[RPL];
     float2 acc[GP][DPL / 2];
@@ -537,79 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
           *reinterpret_cast<float2*>(mine + g * ROWF + 2 + lane * DPL + 2 * k) = acc[g][k];
       named_barrier(kBarConsumers, kConsumerThreads);
 
-      const int64_t c_first = tile_owner(hh * p.tph, p.total_tiles, grid);
-      const int64_t c_last = tile_owner((hh + 1) * p.tph - 1, p.total_tiles, grid);
-      const bool sole = c_first == c_last;
-      const int seg_local = (int)(hh - tb / p.tph);
-      float* slot = p.slots + ((int64_t)blockIdx.x * p.max_seg + seg_local) * GP * ROWF;
-      for (int e = ctid; e < p.Rc * DV; e += kConsumerThreads) {
-        const int r = e / DV, d = e - r * DV;
-        float M = NEG_INF;
-        for (int w = 0; w < kWarps; ++w) M = fmaxf(M, stg[(w * GP + r) * ROWF]);
-        float Lsum = 0.f, A = 0.f;
-        if (M != NEG_INF) {
-          for (int w = 0; w < kWarps; ++w) {
-            const float* src = stg + (w * GP + r) * ROWF;
-            const float sc = fast_exp2((src[0] - M) * kLog2e);
-            Lsum = fmaf(src[1], sc, Lsum);
-            A = fmaf(src[2 + d], sc, A);
-          }
-        }
-        if (sole) {
-          const int64_t orow = hh * p.R + p.r0 + r;
-          if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
-          if (p.partials) {
-            float* pr = p.partials + orow * (int64_t)(DV + 2);
-            pr[2 + d] = A;
-            if (d == 0) { pr[0] = M; pr[1] = Lsum; }
-          }
-        } else {
-          slot[r * ROWF + 2 + d] = A;
-          if (d == 0) { slot[r * ROWF] = M; slot[r * ROWF + 1] = Lsum; }
-        }
-      }
-      if (!sole) {
-        __threadfence();
-        named_barrier(kBarConsumers, kConsumerThreads);
-        if (ctid == 0) {
-          const int n_contrib = (int)(c_last - c_first + 1);
-          const int prev = atomicAdd(&p.counters[hh], 1);
-          flag_s[0] = prev == n_contrib - 1;
-        }
-        named_barrier(kBarConsumers, kConsumerThreads);
-        if (flag_s[0]) {
-          __threadfence();
-          for (int e = ctid; e < p.Rc * DV; e += kConsumerThreads) {
-            const int r = e / DV, d = e - r * DV;
-            float M = NEG_INF, Lsum = 0.f, A = 0.f;
-            for (int64_t c = c_first; c <= c_last; ++c) {
-              const int sl = (int)(hh - tile_start(c, p.total_tiles, grid) / p.tph);
-              const float* src = p.slots + ((c * p.max_seg + sl) * GP + r) * ROWF;
-              const float m = __ldcg(src);
-              if (m == NEG_INF) continue;
-              const float l = __ldcg(src + 1), a = __ldcg(src + 2 + d);
-              if (m > M) {
-                const float sc = fast_exp2((M - m) * kLog2e);
-                Lsum = Lsum * sc + l;
-                A = A * sc + a;
-                M = m;
-              } else {
-                const float sc = fast_exp2((m - M) * kLog2e);
-                Lsum = fmaf(l, sc, Lsum);
-                A = fmaf(a, sc, A);
-              }
-            }
-            const int64_t orow = hh * p.R + p.r0 + r;
-            if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
-            if (p.partials) {
-              float* pr = p.partials + orow * (int64_t)(DV + 2);
-              pr[2 + d] = A;
-              if (d == 0) { pr[0] = M; pr[1] = Lsum; }
-            }
-          }
-          if (ctid == 0) atomicExch(&p.counters[hh], 0);
-        }
-      }
+      finish_segment<GP, DV, kWarps>(p, stg, hh, tb, grid, ctid, flag_s);
     }
     f = fend;
   }

@@ -1,0 +1,564 @@
+// Fused SunShape decode attention for 16-bit values: LUT-gather scores on CUDA
+// cores, softmax . V on the tensor cores.
+//
+// Same persistent split and segment protocol as decode_kernel (decode.cuh); the
+// consumer work per token is reorganised:
+//
+//   * value tiles arrive by TMA tensor copies (cp.async.bulk.tensor, 64 tokens x
+//     64 columns per box, 128-byte swizzle), index / heavy rows by 1-D bulk copies;
+//     the producer also keeps a few tiles beyond the shared-memory ring streaming
+//     into L2 (cp.async.bulk.prefetch) so HBM stays busy while consumers hold stages;
+//   * one lane scores one token against all G query rows of its KV head.  At
+//     step k of its block loop, lane l gathers block 8*kh + ((kl + l) & 7): the 8
+//     lanes of every shared-memory phase read 8 different blocks, and the LUT keeps
+//     block b's 16-byte entries in bank group b & 7, so the 128-bit gathers are
+//     conflict-free and no cross-lane reduction is needed;
+//   * online softmax with a lazy rescale: the running max only moves when a score
+//     exceeds it by more than kLazyTau (rare after the first tile), so most tiles
+//     need no shuffles and no accumulator rescale;
+//   * P (bf16/f16, as the reference casts probabilities to the value dtype before
+//     P @ V, vllm_attn_backend.py:251-252) goes to a token-major shared tile and
+//     acc^T[dv][g] += V^T[dv][t] P^T[t][g] runs as m16n8k16 MMAs with fp32
+//     accumulators, A fragments loaded straight from the swizzled value tile.
+#pragma once
+
+#include "decode.cuh"
+
+namespace sunshape {
+
+constexpr int kWarpsM = 8;                       // consumer warps
+constexpr int kThreadsM = (kWarpsM + 1) * 32;    // + producer warp
+constexpr int kConsumerThreadsM = kWarpsM * 32;
+constexpr int kWarpsPerTileM = kTileTokens / 32; // 2
+constexpr int kTileGroupsM = kWarpsM / kWarpsPerTileM;
+constexpr float kLazyTau = 8.0f;                 // p = exp(s - m) <= e^8 between rescales
+constexpr int kVBoxBytes = 64 * 128;             // one TMA box: 64 tokens x 64 columns x 2 B
+constexpr int kLutC = 256;                       // LUT rows per (block group, half): fixed 256-codeword stride
+constexpr int kPrefetchAhead = 4;                // tiles prefetched into L2 beyond the shared-memory ring
+
+template <typename VT>
+struct MmaOp;
+
+template <>
+struct MmaOp<__nv_bfloat16> {
+  __device__ __forceinline__ static void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  }
+  __device__ __forceinline__ static uint16_t bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+};
+
+template <>
+struct MmaOp<__half> {
+  __device__ __forceinline__ static void mma(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  }
+  __device__ __forceinline__ static uint16_t bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+};
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t (&r)[2], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+// P tile of one warp: 32 token rows x (8 * NT) query rows, 16-bit, token-major.  With two
+// 16-byte chunks per row (NT == 2) the chunk index is XOR-swizzled with bit 2 of the row so
+// the transposed ldmatrix reads of 8 consecutive rows hit 8 different bank groups.
+template <int NT>
+__device__ __forceinline__ uint32_t p_chunk_offset(int row, int chunk) {
+  if constexpr (NT == 1) return (uint32_t)row * 16u;
+  else return (uint32_t)row * 32u + (uint32_t)((chunk ^ ((row >> 2) & 1)) << 4);
+}
+
+// LUT rows of one block for this thread: q block held in registers, codebook rows loaded
+// four at a time so their L2 latencies overlap; stores land in bank group b & 7.
+template <int GP, int BD>
+__device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float* qblk, const float* cbb, bool active,
+                                             uint8_t* dst_base, int c0) {
+  constexpr int NH = GP / 4;
+  float q[GP][BD];
+#pragma unroll
+  for (int g = 0; g < GP; ++g)
+#pragma unroll
+    for (int d = 0; d < BD; ++d) q[g][d] = active ? qblk[g * p.D + d] : 0.f;
+  for (int cb4 = c0; cb4 < p.C; cb4 += 128) {
+    float x[4][BD];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = cb4 + 32 * u;
+#pragma unroll
+      for (int d = 0; d < BD; ++d) x[u][d] = (active && c < p.C) ? __ldg(cbb + (int64_t)c * BD + d) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = cb4 + 32 * u;
+      if (c >= p.C) break;
+      float v[GP];
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        float a = 0.f;
+#pragma unroll
+        for (int d = 0; d < BD; ++d) a = fmaf(q[g][d], x[u][d], a);
+        v[g] = a;
+      }
+#pragma unroll
+      for (int h = 0; h < NH; ++h)
+        *reinterpret_cast<float4*>(dst_base + ((int64_t)h * kLutC + c) * 128) =
+            make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+    }
+  }
+}
+
+// LUT of flat head hh for the tensor-core kernel: 16-byte entry (b, h, c) at
+// ((kh * NH + h) * 256 + c) * 128 + (b & 7) * 16 with kh = b / 8, holding q rows 4h..4h+3.
+// Heavy and padding blocks get zero rows (their stored index is 0).
+template <int GP>
+__device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
+                            float* q_s, uint8_t* lut, int ctid) {
+  constexpr int NH = GP / 4;
+  named_barrier(kBarConsumers, kConsumerThreadsM);
+  for (int e = ctid; e < GP * p.D; e += kConsumerThreadsM) {
+    const int g = e / p.D, dp = e - g * p.D;
+    float v = 0.f;
+    if (g < p.Rc) {
+      const int64_t qrow = hh * p.R + p.r0 + g;
+      float x = load_as_float(p.q, qrow * p.D + perm_s[dp], p.q_dtype);
+      if (p.has_scale) x = round_to_dtype(x * p.scale, p.q_dtype);
+      v = x;
+    }
+    q_s[g * p.D + dp] = v;
+  }
+  named_barrier(kBarConsumers, kConsumerThreadsM);
+  const int cbh = p.n_cb == 1 ? 0 : (int)((hh % p.kv_heads) % p.n_cb);
+  const float* cb = p.cb + (int64_t)cbh * p.nb * p.C * p.bd;
+  const int blo = ctid & 7, c0 = ctid >> 3;   // 8 bank groups x 32 codeword lanes
+  for (int kh = 0; kh < p.nbh; ++kh) {
+    const int b = blo + 8 * kh;
+    const bool active = b < p.nb && hslot_s[b] < 0;
+    const float* qblk = q_s + (active ? b : 0) * p.bd;
+    const float* cbb = cb + (int64_t)(active ? b : 0) * p.C * p.bd;
+    uint8_t* dst = lut + (int64_t)kh * NH * kLutC * 128 + blo * 16;
+    if (p.bd == 8) {
+      lut_rows_reg<GP, 8>(p, qblk, cbb, active, dst, c0);
+    } else if (p.bd == 4) {
+      lut_rows_reg<GP, 4>(p, qblk, cbb, active, dst, c0);
+    } else {
+      for (int c = c0; c < p.C; c += 32) {
+        float v[GP];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) v[g] = 0.f;
+        if (active)
+          for (int d = 0; d < p.bd; ++d) {
+            const float x = __ldg(cbb + (int64_t)c * p.bd + d);
+#pragma unroll
+            for (int g = 0; g < GP; ++g) v[g] = fmaf(qblk[g * p.D + d], x, v[g]);
+          }
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+          *reinterpret_cast<float4*>(dst + ((int64_t)h * kLutC + c) * 128) =
+              make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+      }
+    }
+  }
+  named_barrier(kBarConsumers, kConsumerThreadsM);
+}
+
+// Producer warp of the tensor-core kernel: TMA tensor boxes for values, bulk
+// copies (+ byte tails) for index and heavy rows, L2 prefetch ahead of the ring.
+template <int DV>
+__device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint64_t* full, uint64_t* empty,
+                            uint8_t* stage0, int n_heavy, int lane) {
+  const int S = p.stages;
+  const int64_t hrow = (int64_t)n_heavy * p.bd * (p.heavy_dtype == SUNSHAPE_F32 ? 4 : 2);
+  constexpr int NBOX = DV / 64;
+  const int64_t n_tiles = te - tb;
+  auto prefetch_tile = [&](int64_t i) {
+    if (lane != 0 || i >= n_tiles) return;
+    const int64_t f = tb + i;
+    const int64_t hh = f / p.tph;
+    const int t0 = (int)(f - hh * p.tph) * kTileTokens;
+    const int ntok = min(kTileTokens, p.T - t0);
+    const int64_t row0 = hh * p.head_stride + t0;
+    prefetch_l2(reinterpret_cast<const uint8_t*>(p.v) + row0 * DV * 2, (uint32_t)ntok * DV * 2);
+    const uintptr_t a0 = (reinterpret_cast<uintptr_t>(p.idx + row0 * p.nb) + 15) & ~uintptr_t(15);
+    const uintptr_t a1 = reinterpret_cast<uintptr_t>(p.idx + (row0 + ntok) * p.nb) & ~uintptr_t(15);
+    if (a1 > a0) prefetch_l2(reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0));
+  };
+  for (int64_t i = 0; i < n_tiles && i < S + kPrefetchAhead; ++i) prefetch_tile(i);
+  for (int64_t i = 0; i < n_tiles; ++i) {
+    const int s = (int)(i % S);
+    if (i >= S) {
+      mbar_wait(&empty[s], (uint32_t)(((i / S) - 1) & 1), p.err, kErrWaitEmpty);
+      prefetch_tile(i + kPrefetchAhead);
+    }
+    const int64_t f = tb + i;
+    const int64_t hh = f / p.tph;
+    const int t0 = (int)(f - hh * p.tph) * kTileTokens;
+    const int ntok = min(kTileTokens, p.T - t0);
+    const int64_t row0 = hh * p.head_stride + t0;
+    uint8_t* st = stage0 + (int64_t)s * p.stage_bytes;
+
+    const uint8_t* isrc = p.idx + row0 * p.nb;
+    const int64_t ilen = (int64_t)ntok * p.nb;
+    const uintptr_t ia0 = reinterpret_cast<uintptr_t>(isrc) & ~uintptr_t(15);
+    const uintptr_t ia1 = (reinterpret_cast<uintptr_t>(isrc) + ilen) & ~uintptr_t(15);
+    const uint32_t ibulk = ia1 > ia0 ? (uint32_t)(ia1 - ia0) : 0u;
+    {
+      const uintptr_t tail0 = max(ia1, reinterpret_cast<uintptr_t>(isrc));
+      const int ntail = (int)(reinterpret_cast<uintptr_t>(isrc) + ilen - tail0);
+      if (lane < ntail)
+        st[p.off_stage_idx + (tail0 - ia0) + lane] = *reinterpret_cast<const uint8_t*>(tail0 + lane);
+    }
+    uint32_t hbulk = 0;
+    uintptr_t ha0 = 0;
+    if (n_heavy > 0) {
+      const uint8_t* hsrc = reinterpret_cast<const uint8_t*>(p.heavy) + row0 * hrow;
+      const int64_t hlen = (int64_t)ntok * hrow;
+      ha0 = reinterpret_cast<uintptr_t>(hsrc) & ~uintptr_t(15);
+      const uintptr_t ha1 = (reinterpret_cast<uintptr_t>(hsrc) + hlen) & ~uintptr_t(15);
+      hbulk = ha1 > ha0 ? (uint32_t)(ha1 - ha0) : 0u;
+      const uintptr_t tail0 = max(ha1, reinterpret_cast<uintptr_t>(hsrc));
+      const int ntail = (int)(reinterpret_cast<uintptr_t>(hsrc) + hlen - tail0);
+      if (lane < ntail)
+        st[p.off_stage_heavy + (tail0 - ha0) + lane] = *reinterpret_cast<const uint8_t*>(tail0 + lane);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&full[s], NBOX * kVBoxBytes + ibulk + hbulk);
+#pragma unroll
+      for (int bx = 0; bx < NBOX; ++bx) tma_load_2d(st + bx * kVBoxBytes, &p.tmap_v, bx * 64, (int)row0, &full[s]);
+      if (ibulk) bulk_g2s(st + p.off_stage_idx, reinterpret_cast<const void*>(ia0), ibulk, &full[s]);
+      if (hbulk) bulk_g2s(st + p.off_stage_heavy, reinterpret_cast<const void*>(ha0), hbulk, &full[s]);
+    }
+    __syncwarp();
+  }
+}
+
+template <int GP, int DV, typename VT>
+__global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_constant__ DecodeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 128B-swizzled TMA boxes need 1024-byte aligned destinations: align the carve-up base
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  constexpr int NH = GP / 4;          // 16-byte LUT halves per (block, codeword)
+  constexpr int NT = (GP + 7) / 8;    // MMA n-tiles (8 query rows each)
+  constexpr int MT = DV / 16;         // MMA m-tiles (16 value columns each)
+  using Op = MmaOp<VT>;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + kMaxStages;
+  int* flag_s = reinterpret_cast<int*>(smem + 128);
+  int* perm_s = reinterpret_cast<int*>(smem + p.off_perm);
+  int8_t* hslot_s = reinterpret_cast<int8_t*>(smem + p.off_hslot);
+  int8_t* hlist_s = hslot_s + 32;                 // heavy block ids in slot order
+  float* q_s = reinterpret_cast<float*>(smem + p.off_q);
+  uint8_t* pbuf = smem + p.off_p;
+  uint8_t* lut = smem + p.off_lut;
+  uint8_t* stage0 = smem + p.off_stage;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t grid = gridDim.x;
+  const int64_t tb = tile_start(blockIdx.x, p.total_tiles, grid);
+  const int64_t te = tile_start(blockIdx.x + 1, p.total_tiles, grid);
+
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarpsPerTileM);
+    }
+    fence_mbar_init();
+    int n = 0;
+    for (int b = 0; b < p.nb; ++b) {
+      const bool h = p.heavy_mask != nullptr && p.heavy_mask[b] != 0;
+      hslot_s[b] = h ? (int8_t)n : (int8_t)-1;
+      if (h) hlist_s[n++] = (int8_t)b;
+    }
+    flag_s[2] = n;
+  }
+  for (int i = tid; i < p.D; i += kThreadsM) perm_s[i] = (int)p.perm[i];
+  __syncthreads();
+  const int n_heavy = flag_s[2];
+  if (te <= tb) return;
+
+  if (warp == kWarpsM) {
+    produce_mma<DV>(p, tb, te, full, empty, stage0, n_heavy, lane);
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const int ctid = tid;
+  const int tg = warp / kWarpsPerTileM, half = warp % kWarpsPerTileM;
+  uint8_t* pw = pbuf + warp * (NT * 512 + 64);      // [32 tokens][8*NT rows] 16-bit P tile
+  float* alpha_s = reinterpret_cast<float*>(pw + NT * 512);
+  const uint32_t pw_u32 = smem_u32(pw);
+  const int hsize = p.heavy_dtype == SUNSHAPE_F32 ? 4 : 2;
+  const int64_t hrow = (int64_t)n_heavy * p.bd * hsize;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  const bool fast_idx = (p.nb & 7) == 0;
+  const int gid = lane >> 2, tig = lane & 3;
+
+  int64_t f = tb;
+  while (f < te) {
+    const int64_t hh = f / p.tph;
+    const int64_t fend = min(te, (hh + 1) * p.tph);
+    const int i0 = (int)(f - tb), i1 = (int)(fend - tb);
+    build_lut_m<GP>(p, hh, perm_s, hslot_s, q_s, lut, ctid);
+
+    float m_run[GP], l_run[GP];
+    float acc[MT][NT][4];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) { m_run[g] = NEG_INF; l_run[g] = 0.f; }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[mt][nt][c] = 0.f;
+
+    const int64_t b_idx = hh / p.kv_heads;
+    const int kvh = (int)(hh % p.kv_heads);
+
+    for (int i = i0 + ((tg - i0 % kTileGroupsM) + kTileGroupsM) % kTileGroupsM; i < i1; i += kTileGroupsM) {
+      const int s = i % p.stages;
+      mbar_wait(&full[s], (uint32_t)((i / p.stages) & 1), p.err, kErrWaitFull);
+      const int64_t ft = tb + i;
+      const int t0 = (int)(ft - hh * p.tph) * kTileTokens;
+      const int ntok = min(kTileTokens, p.T - t0);
+      const int64_t row0 = hh * p.head_stride + t0;
+      uint8_t* st = stage0 + (int64_t)s * p.stage_bytes;
+      const uint8_t* itile = st + p.off_stage_idx + (reinterpret_cast<uintptr_t>(p.idx + row0 * p.nb) & 15);
+      const uint8_t* htile = st + p.off_stage_heavy;
+      if (n_heavy > 0)
+        htile += reinterpret_cast<uintptr_t>(reinterpret_cast<const uint8_t*>(p.heavy) + row0 * hrow) & 15;
+      const int tok0 = half * 32;
+      const int t = tok0 + lane;
+      const bool valid = t < ntok;
+
+      if (tok0 < ntok) {
+        // tail tile: rows past the sequence may hold stale cache data -> zero them (p is 0 there)
+        if (ntok < tok0 + 32) {
+          for (int e = lane; e < (tok0 + 32 - ntok) * (DV / 8); e += 32) {
+            const int rr = ntok + e / (DV / 8), ch = e % (DV / 8);
+            *reinterpret_cast<uint4*>(st + (ch >> 3) * kVBoxBytes + rr * 128 + ((ch & 7) << 4)) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+        }
+        // ---- scores: lane t against all GP rows
+        float2 part[GP / 2];
+#pragma unroll
+        for (int g = 0; g < GP / 2; ++g) part[g] = make_float2(0.f, 0.f);
+        if (valid) {
+          const uint8_t* irow = itile + t * p.nb;
+          const int rot = lane & 7;
+#pragma unroll
+          for (int kh = 0; kh < 4; ++kh) {
+            if (kh >= p.nbh) break;
+            uint64_t w;
+            if (fast_idx) {
+              w = *reinterpret_cast<const uint64_t*>(irow + 8 * kh);
+            } else {
+              w = 0;
+              for (int q = 0; q < 8; ++q) {
+                const int b = 8 * kh + q;
+                if (b < p.nb) w |= (uint64_t)irow[b] << (8 * q);
+              }
+            }
+            // rotate so byte kl of w holds block 8*kh + ((kl + lane) & 7)
+            const uint64_t wr = rot ? ((w >> (8 * rot)) | (w << (64 - 8 * rot))) : w;
+            const uint32_t lo = (uint32_t)wr, hi = (uint32_t)(wr >> 32);
+            const uint8_t* kbase = lut + kh * NH * kLutC * 128;
+#pragma unroll
+            for (int kl = 0; kl < 8; ++kl) {
+              const uint32_t c = ((kl < 4 ? lo : hi) >> (8 * (kl & 3))) & 0xffu;
+              const uint8_t* e = kbase + c * 128u + (uint32_t)(((kl + lane) & 7) << 4);
+#pragma unroll
+              for (int h = 0; h < NH; ++h) {
+                const float4 v = *reinterpret_cast<const float4*>(e + h * kLutC * 128);
+                part[2 * h] = __fadd2_rn(part[2 * h], make_float2(v.x, v.y));
+                part[2 * h + 1] = __fadd2_rn(part[2 * h + 1], make_float2(v.z, v.w));
+              }
+            }
+          }
+          // SunShape-Mixed heavy blocks: dense dot of the stored block with the permuted query
+          for (int hs = 0; hs < n_heavy; ++hs) {
+            const int b = hlist_s[hs];
+            const uint8_t* hv = htile + ((int64_t)t * n_heavy + hs) * p.bd * hsize;
+            const float* qb = q_s + b * p.bd;
+            for (int d = 0; d < p.bd; ++d) {
+              const float x = hsize == 4 ? reinterpret_cast<const float*>(hv)[d]
+                                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(hv)[d]);
+#pragma unroll
+              for (int g = 0; g < GP / 2; ++g) {
+                part[g].x = fmaf(qb[(2 * g) * p.D + d], x, part[g].x);
+                part[g].y = fmaf(qb[(2 * g + 1) * p.D + d], x, part[g].y);
+              }
+            }
+          }
+        }
+        float sc[GP];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+          float v = valid ? ((g & 1) ? part[g >> 1].y : part[g >> 1].x) : NEG_INF;
+          if (valid && p.mask != nullptr && g < p.Rc) {
+            const int r = p.r0 + g;
+            const int gq = r / p.L, ql = r - gq * p.L;
+            const int64_t hq = (int64_t)kvh * p.G + gq;
+            v += load_as_float(p.mask, b_idx * p.msb + hq * p.msh + ql * p.msq + (t0 + t), p.mask_dtype);
+          }
+          sc[g] = v;
+        }
+        // ---- online softmax with lazy rescale
+        bool need = false;
+#pragma unroll
+        for (int g = 0; g < GP; ++g) need |= sc[g] > m_run[g] + kLazyTau;
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int g = 0; g < GP; ++g) {
+            const float mn = fmaxf(m_run[g], warp_max(sc[g]));
+            const float a = (mn == NEG_INF) ? 1.f : fast_exp2((m_run[g] - mn) * kLog2e);
+            m_run[g] = mn;
+            l_run[g] *= a;
+            if (lane == 0) alpha_s[g] = a;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const int g0 = nt * 8 + 2 * tig;
+            const float a0 = g0 < GP ? alpha_s[g0] : 1.f, a1 = g0 + 1 < GP ? alpha_s[g0 + 1] : 1.f;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+              acc[mt][nt][0] *= a0; acc[mt][nt][1] *= a1; acc[mt][nt][2] *= a0; acc[mt][nt][3] *= a1;
+            }
+          }
+        }
+        uint32_t pk[NT * 4];   // this token's P row, packed 16-bit pairs
+#pragma unroll
+        for (int g2 = 0; g2 < NT * 4; ++g2) pk[g2] = 0u;
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+          const float pr = (m_run[g] == NEG_INF) ? 0.f : fast_exp2((sc[g] - m_run[g]) * kLog2e);
+          l_run[g] += pr;
+          pk[g >> 1] |= (uint32_t)Op::bits(pr) << (16 * (g & 1));
+        }
+#pragma unroll
+        for (int ch = 0; ch < NT; ++ch)
+          *reinterpret_cast<uint4*>(pw + p_chunk_offset<NT>(lane, ch)) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+        __syncwarp();
+        // ---- acc^T[dv][g] += V^T[dv][t] . P^T[t][g] over this warp's 32 tokens
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          // B fragments (P^T, k = token, n = query row) from the token-major P tile via transposed ldmatrix
+          uint32_t bfrag[NT][2];
+          {
+            const int prow = ks * 16 + (lane & 15);
+            if constexpr (NT == 1) {
+              ldsm_x2_trans(bfrag[0], pw_u32 + p_chunk_offset<1>(prow, 0));
+            } else {
+              uint32_t r4[4];
+              ldsm_x4_trans(r4, pw_u32 + p_chunk_offset<2>(prow, lane >> 4));
+              bfrag[0][0] = r4[0]; bfrag[0][1] = r4[1]; bfrag[1][0] = r4[2]; bfrag[1][1] = r4[3];
+            }
+          }
+          const int mi = lane >> 3;
+          const int trow = tok0 + ks * 16 + ((mi >> 1) << 3) + (lane & 7);   // token row of the V tile
+          const uint32_t vrow = smem_u32(st) + (uint32_t)trow * 128u;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            const int dv = mt * 16 + ((mi & 1) << 3);
+            const int ch = (dv & 63) >> 3;
+            uint32_t afrag[4];
+            ldsm_x4_trans(afrag, vrow + (uint32_t)(dv >> 6) * kVBoxBytes + (uint32_t)((ch ^ (trow & 7)) << 4));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) Op::mma(acc[mt][nt], afrag, bfrag[nt]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ---------------- segment end: per-warp partials -> staging -> merge
+    float l_tot[GP];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) l_tot[g] = warp_sum(l_run[g]);
+    named_barrier(kBarConsumers, kConsumerThreadsM);   // LUT reads done: reuse it as staging
+    constexpr int ROWF = DV + 2;
+    float* stg = reinterpret_cast<float*>(lut);
+    float* mine = stg + warp * GP * ROWF;
+    if (lane == 0) {
+#pragma unroll
+      for (int g = 0; g < GP; ++g) { mine[g * ROWF] = m_run[g]; mine[g * ROWF + 1] = l_tot[g]; }
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int g0 = nt * 8 + 2 * tig, dv0 = mt * 16 + gid;
+        if (g0 < GP) {
+          mine[g0 * ROWF + 2 + dv0] = acc[mt][nt][0];
+          mine[g0 * ROWF + 2 + dv0 + 8] = acc[mt][nt][2];
+        }
+        if (g0 + 1 < GP) {
+          mine[(g0 + 1) * ROWF + 2 + dv0] = acc[mt][nt][1];
+          mine[(g0 + 1) * ROWF + 2 + dv0 + 8] = acc[mt][nt][3];
+        }
+      }
+    named_barrier(kBarConsumers, kConsumerThreadsM);
+    finish_segment<GP, DV, kWarpsM>(p, stg, hh, tb, grid, ctid, flag_s);
+    f = fend;
+  }
+}
+
+template <int GP, int DV, typename VT>
+void launch_decode_mma_t(const DecodeLaunch& l, cudaStream_t st) {
+  auto k = decode_mma_kernel<GP, DV, VT>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem);
+  k<<<(unsigned)l.grid, kThreadsM, l.smem, st>>>(l.prm);
+}
+
+
+// Instantiated in decode_mma_bf16.cu / decode_mma_f16.cu.
+extern template void launch_decode_mma_t<4, 64, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 128, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 256, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 64, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 128, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 256, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 64, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 128, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 256, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 64, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 128, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 256, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 64, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 128, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 256, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 64, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 128, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 256, __half>(const DecodeLaunch&, cudaStream_t);
+
+}  // namespace sunshape

@@ -70,7 +70,7 @@ def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, 
     idx = quantized_key.indices
     if idx.dtype != torch.uint8:
         idx = idx.to(torch.uint8)
-    idx = idx.contiguous()
+    idx = _lib.aligned16(idx.contiguous())
     heavy = _heavy_compact(codec, quantized_key) if n_heavy else None
     q = query.contiguous()
     if q.dtype not in (torch.float32, torch.bfloat16, torch.float16):

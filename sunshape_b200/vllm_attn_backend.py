@@ -184,9 +184,12 @@ def dequantize_keys(codec, keys: SunShapeQuantizedKeys) -> torch.Tensor:
     idx, heavy = keys.packed(codec)
     B, H, T = keys.batch_size, keys.num_kv_heads, keys.seq_len
     idx_c, hs = _heads_view(idx, B, H, T)
+    idx_c = _lib.aligned16(idx_c)
+    if idx_c is not idx and hs != T:
+        idx_c, hs = _lib.aligned16(idx.contiguous()), T
     heavy_c = None
     if heavy is not None:
-        heavy_c = heavy.contiguous() if not _same_head_stride(heavy, hs, T) else heavy
+        heavy_c = _lib.aligned16(heavy.contiguous() if not _same_head_stride(heavy, hs, T) else heavy)
     out = torch.empty(B, H, T, codec.head_dim, device=idx.device, dtype=torch.float32)
     if B * H * T:
         kd = _lib.kv_desc(idx_c, heavy_c, None, T, hs)
@@ -299,9 +302,11 @@ def _heads_view(t: torch.Tensor, B: int, H: int, T: int) -> tuple[torch.Tensor, 
 def _kv_layout(value, idx, heavy, B, H, T):
     """Pick one head stride (tokens) shared by values, indices and heavy rows; copy if they disagree."""
     v, hs = _heads_view(value, B, H, T)
-    if _same_head_stride(idx, hs, T) and (heavy is None or _same_head_stride(heavy, hs, T)):
+    aligned = all(t is None or t.data_ptr() % 16 == 0 for t in (v, idx, heavy))
+    if aligned and _same_head_stride(idx, hs, T) and (heavy is None or _same_head_stride(heavy, hs, T)):
         return v, idx, heavy, hs
-    return value.contiguous(), idx.contiguous(), (heavy.contiguous() if heavy is not None else None), T
+    return (_lib.aligned16(value.contiguous()), _lib.aligned16(idx.contiguous()),
+            (_lib.aligned16(heavy.contiguous()) if heavy is not None else None), T)
 
 
 def _apply_quantized_attention(*, codec, query: torch.Tensor, key: SunShapeQuantizedKeys, value: torch.Tensor,

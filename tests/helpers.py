@@ -35,15 +35,15 @@ def make_codec(perm, centroids, heavy_mask, head_dim, block_dim, n_centroids, de
     """SunShapeBlockCodec with per-KV-head codebooks written directly (no fitting)."""
     from sunshape_b200.codec import SunShapeBlockCodec
 
-    perm = torch.as_tensor(perm, dtype=torch.long)
-    cents = torch.as_tensor(centroids, dtype=torch.float32)
-    heavy = torch.as_tensor(heavy_mask, dtype=torch.bool)
+    perm = torch.as_tensor(perm, dtype=torch.long).cpu()
+    cents = torch.as_tensor(centroids, dtype=torch.float32).cpu()
+    heavy = torch.as_tensor(heavy_mask, dtype=torch.bool).cpu()
     mode = "profileperm_mixed_precision" if bool(heavy.any()) else "profileperm_baseline"
     codec = SunShapeBlockCodec(head_dim=head_dim, block_dim=block_dim, n_centroids=n_centroids, mode=mode,
                                device=torch.device(device), kv_heads=cents.shape[0] if cents.ndim == 4 else None)
     codec.permutation.copy_(perm)
     inv = torch.empty_like(perm)
-    inv[perm] = torch.arange(len(perm))
+    inv[perm] = torch.arange(len(perm), device=perm.device)
     codec.inv_permutation.copy_(inv)
     codec.centroids.copy_(cents)
     codec.mixed_high_precision_blocks.copy_(heavy)
