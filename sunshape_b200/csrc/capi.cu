@@ -1,6 +1,7 @@
 // extern "C" boundary of libsunshape_b200.so: argument validation with
 // reference-style reason strings, template dispatch and launch configuration.
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -195,6 +196,8 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
       pl.smem = off_stage + stages * stage_bytes + 1024;
       DecodeParams& p = pl.prm;
       p.stages = stages;
+      const char* pf = std::getenv("SUNSHAPE_L2_PREFETCH");
+      p.prefetch_ahead = pf ? std::max(0, std::atoi(pf)) : kPrefetchAhead;
       p.stage_bytes = stage_bytes;
       p.off_stage_idx = vpart;
       p.off_stage_heavy = vpart + ipart;

@@ -93,6 +93,7 @@ struct DecodeParams {
   int max_seg;
   // shared memory carve-up (bytes)
   int stages;
+  int prefetch_ahead;   // tiles streamed into L2 beyond the ring (tensor-core kernel)
   int stage_bytes;
   int off_stage_idx;
   int off_stage_heavy;

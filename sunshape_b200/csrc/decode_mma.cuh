@@ -34,7 +34,7 @@ constexpr int kTileGroupsM = kWarpsM / kWarpsPerTileM;
 constexpr float kLazyTau = 8.0f;                 // p = exp(s - m) <= e^8 between rescales
 constexpr int kVBoxBytes = 64 * 128;             // one TMA box: 64 tokens x 64 columns x 2 B
 constexpr int kLutC = 256;                       // LUT rows per (block group, half): fixed 256-codeword stride
-constexpr int kPrefetchAhead = 4;                // tiles prefetched into L2 beyond the shared-memory ring
+constexpr int kPrefetchAhead = 0;                // tiles prefetched into L2 beyond the ring (measured: off is fastest)
 
 template <typename VT>
 struct MmaOp;
@@ -194,28 +194,36 @@ __device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint6
   const int64_t hrow = (int64_t)n_heavy * p.bd * (p.heavy_dtype == SUNSHAPE_F32 ? 4 : 2);
   constexpr int NBOX = DV / 64;
   const int64_t n_tiles = te - tb;
-  auto prefetch_tile = [&](int64_t i) {
-    if (lane != 0 || i >= n_tiles) return;
-    const int64_t f = tb + i;
-    const int64_t hh = f / p.tph;
-    const int t0 = (int)(f - hh * p.tph) * kTileTokens;
-    const int ntok = min(kTileTokens, p.T - t0);
-    const int64_t row0 = hh * p.head_stride + t0;
-    prefetch_l2(reinterpret_cast<const uint8_t*>(p.v) + row0 * DV * 2, (uint32_t)ntok * DV * 2);
-    const uintptr_t a0 = (reinterpret_cast<uintptr_t>(p.idx + row0 * p.nb) + 15) & ~uintptr_t(15);
-    const uintptr_t a1 = reinterpret_cast<uintptr_t>(p.idx + (row0 + ntok) * p.nb) & ~uintptr_t(15);
-    if (a1 > a0) prefetch_l2(reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0));
-  };
-  for (int64_t i = 0; i < n_tiles && i < S + kPrefetchAhead; ++i) prefetch_tile(i);
-  for (int64_t i = 0; i < n_tiles; ++i) {
-    const int s = (int)(i % S);
-    if (i >= S) {
-      mbar_wait(&empty[s], (uint32_t)(((i / S) - 1) & 1), p.err, kErrWaitEmpty);
-      prefetch_tile(i + kPrefetchAhead);
+  const int ahead = p.prefetch_ahead;
+  // tile cursors advance incrementally (no 64-bit divisions on the issue path)
+  int64_t hh = tb / p.tph;
+  int t0 = (int)(tb - hh * p.tph) * kTileTokens;
+  int64_t ph_h = hh;   // prefetch cursor
+  int ph_t0 = t0;
+  int64_t n_pref = 0;
+  auto prefetch_next = [&]() {
+    if (n_pref >= n_tiles) return;
+    if (lane == 0) {
+      const int ntok = min(kTileTokens, p.T - ph_t0);
+      const int64_t row0 = ph_h * p.head_stride + ph_t0;
+      prefetch_l2(reinterpret_cast<const uint8_t*>(p.v) + row0 * DV * 2, (uint32_t)ntok * DV * 2);
+      const uintptr_t a0 = (reinterpret_cast<uintptr_t>(p.idx + row0 * p.nb) + 15) & ~uintptr_t(15);
+      const uintptr_t a1 = reinterpret_cast<uintptr_t>(p.idx + (row0 + ntok) * p.nb) & ~uintptr_t(15);
+      if (a1 > a0) prefetch_l2(reinterpret_cast<const void*>(a0), (uint32_t)(a1 - a0));
     }
-    const int64_t f = tb + i;
-    const int64_t hh = f / p.tph;
-    const int t0 = (int)(f - hh * p.tph) * kTileTokens;
+    ++n_pref;
+    ph_t0 += kTileTokens;
+    if (ph_t0 >= p.T) { ph_t0 = 0; ++ph_h; }
+  };
+  if (ahead > 0)
+    while (n_pref < S + ahead && n_pref < n_tiles) prefetch_next();
+  int s = 0;
+  uint32_t phase = 0;
+  for (int64_t i = 0; i < n_tiles; ++i) {
+    if (i >= S) {
+      mbar_wait(&empty[s], phase ^ 1u, p.err, kErrWaitEmpty);
+      if (ahead > 0) prefetch_next();
+    }
     const int ntok = min(kTileTokens, p.T - t0);
     const int64_t row0 = hh * p.head_stride + t0;
     uint8_t* st = stage0 + (int64_t)s * p.stage_bytes;
@@ -253,6 +261,9 @@ __device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint6
       if (hbulk) bulk_g2s(st + p.off_stage_heavy, reinterpret_cast<const void*>(ha0), hbulk, &full[s]);
     }
     __syncwarp();
+    t0 += kTileTokens;
+    if (t0 >= p.T) { t0 = 0; ++hh; }
+    if (++s == S) { s = 0; phase ^= 1u; }
   }
 }
 
@@ -339,11 +350,13 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
     const int64_t b_idx = hh / p.kv_heads;
     const int kvh = (int)(hh % p.kv_heads);
 
-    for (int i = i0 + ((tg - i0 % kTileGroupsM) + kTileGroupsM) % kTileGroupsM; i < i1; i += kTileGroupsM) {
-      const int s = i % p.stages;
-      mbar_wait(&full[s], (uint32_t)((i / p.stages) & 1), p.err, kErrWaitFull);
-      const int64_t ft = tb + i;
-      const int t0 = (int)(ft - hh * p.tph) * kTileTokens;
+    const int ifirst = i0 + ((tg - i0 % kTileGroupsM) + kTileGroupsM) % kTileGroupsM;
+    int s = ifirst % p.stages;
+    uint32_t phase = (uint32_t)((ifirst / p.stages) & 1);
+    const int64_t seg_tile0 = hh * p.tph;
+    for (int i = ifirst; i < i1; i += kTileGroupsM) {
+      mbar_wait(&full[s], phase, p.err, kErrWaitFull);
+      const int t0 = (int)(tb + i - seg_tile0) * kTileTokens;
       const int ntok = min(kTileTokens, p.T - t0);
       const int64_t row0 = hh * p.head_stride + t0;
       uint8_t* st = stage0 + (int64_t)s * p.stage_bytes;
@@ -499,6 +512,8 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+      s += kTileGroupsM;
+      while (s >= p.stages) { s -= p.stages; phase ^= 1u; }
     }
 
     // ---------------- segment end: per-warp partials -> staging -> merge
