@@ -40,15 +40,18 @@ def is_stale() -> bool:
     return any(os.path.getmtime(d) > lib_m for d in deps if os.path.exists(d))
 
 
-def build(verbose: bool = False, force: bool = False) -> str:
-    if not force and not is_stale():
+def build(verbose: bool = False, force: bool = False, out: str | None = None,
+          defines: tuple[str, ...] = ()) -> str:
+    """Compile the library (to ``out``, default in-tree) with optional -D defines."""
+    lib_path = out or LIB_PATH
+    if not force and not defines and out is None and not is_stale():
         return LIB_PATH
     from concurrent.futures import ThreadPoolExecutor
 
-    obj_dir = os.path.join(ROOT, "_build")
+    obj_dir = os.path.join(ROOT, "_build", "-".join(defines) or "default")
     os.makedirs(obj_dir, exist_ok=True)
     common = [nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
-              "-I", os.path.join(ROOT, "include")]
+              "-I", os.path.join(ROOT, "include"), *[f"-D{d}" for d in defines]]
     if verbose:
         common.append("-Xptxas=-v")
 
@@ -63,15 +66,17 @@ def build(verbose: bool = False, force: bool = False) -> str:
 
     with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 4)) as ex:
         objs = list(ex.map(compile_one, SOURCES))
-    link = [nvcc(), *ARCH_FLAGS, "--shared", "-cudart", "static", *objs, "-o", LIB_PATH + ".tmp"]
+    link = [nvcc(), *ARCH_FLAGS, "--shared", "-cudart", "static", *objs, "-o", lib_path + ".tmp"]
     subprocess.run(link, check=True)
-    os.replace(LIB_PATH + ".tmp", LIB_PATH)
-    return LIB_PATH
+    os.replace(lib_path + ".tmp", lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--out", default=None, help="output path (default: in-tree library)")
+    ap.add_argument("--define", action="append", default=[], help="extra -D define (e.g. SUNSHAPE_TRACE)")
     a = ap.parse_args()
-    print(build(verbose=a.verbose, force=a.force))
+    print(build(verbose=a.verbose, force=a.force, out=a.out, defines=tuple(a.define)))

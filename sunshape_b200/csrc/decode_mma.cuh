@@ -27,7 +27,8 @@
 namespace sunshape {
 
 constexpr int kWarpsM = 8;                       // consumer warps
-constexpr int kThreadsM = (kWarpsM + 1) * 32;    // + producer warp
+constexpr int kProducersM = 2;                   // producer warps, interleaving tiles
+constexpr int kThreadsM = (kWarpsM + kProducersM) * 32;
 constexpr int kConsumerThreadsM = kWarpsM * 32;
 constexpr int kWarpsPerTileM = kTileTokens / 32; // 2
 constexpr int kTileGroupsM = kWarpsM / kWarpsPerTileM;
@@ -35,6 +36,18 @@ constexpr float kLazyTau = 8.0f;                 // p = exp(s - m) <= e^8 betwee
 constexpr int kVBoxBytes = 64 * 128;             // one TMA box: 64 tokens x 64 columns x 2 B
 constexpr int kLutC = 256;                       // LUT rows per (block group, half): fixed 256-codeword stride
 constexpr int kPrefetchAhead = 0;                // tiles prefetched into L2 beyond the ring (measured: off is fastest)
+
+// Opt-in cycle accounting (built only with -DSUNSHAPE_TRACE): per-CTA counters summed into
+// the 64-bit words at workspace offset 64: [0] producer total, [1] producer waiting on empty
+// stages, [2] consumer total (sum over warps), [3] consumer waiting on full stages,
+// [4] consumer LUT builds, [5] consumer segment ends, [6] producer issuing copies.
+#ifdef SUNSHAPE_TRACE
+#define SUNSHAPE_TRACE_ADD(slot, v) atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(p.err) + 64) + (slot), (unsigned long long)(v))
+#define SUNSHAPE_CLK() clock64()
+#else
+#define SUNSHAPE_TRACE_ADD(slot, v) ((void)0)
+#define SUNSHAPE_CLK() 0ll
+#endif
 
 template <typename VT>
 struct MmaOp;
@@ -189,15 +202,16 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
 // copies (+ byte tails) for index and heavy rows, L2 prefetch ahead of the ring.
 template <int DV>
 __device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint64_t* full, uint64_t* empty,
-                            uint8_t* stage0, int n_heavy, int lane) {
+                            uint8_t* stage0, int n_heavy, int lane, int pid) {
   const int S = p.stages;
   const int64_t hrow = (int64_t)n_heavy * p.bd * (p.heavy_dtype == SUNSHAPE_F32 ? 4 : 2);
   constexpr int NBOX = DV / 64;
   const int64_t n_tiles = te - tb;
   const int ahead = p.prefetch_ahead;
-  // tile cursors advance incrementally (no 64-bit divisions on the issue path)
-  int64_t hh = tb / p.tph;
-  int t0 = (int)(tb - hh * p.tph) * kTileTokens;
+  // this warp issues tiles pid, pid + kProducersM, ...; cursors advance incrementally
+  // (no 64-bit divisions on the issue path)
+  int64_t hh = (tb + pid) / p.tph;
+  int t0 = (int)(tb + pid - hh * p.tph) * kTileTokens;
   int64_t ph_h = hh;   // prefetch cursor
   int ph_t0 = t0;
   int64_t n_pref = 0;
@@ -215,14 +229,21 @@ __device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint6
     ph_t0 += kTileTokens;
     if (ph_t0 >= p.T) { ph_t0 = 0; ++ph_h; }
   };
-  if (ahead > 0)
+  if (ahead > 0 && pid == 0)
     while (n_pref < S + ahead && n_pref < n_tiles) prefetch_next();
-  int s = 0;
-  uint32_t phase = 0;
-  for (int64_t i = 0; i < n_tiles; ++i) {
+  int s = pid % S;
+  uint32_t phase = (uint32_t)((pid / S) & 1);
+  const long long tp0 = SUNSHAPE_CLK();
+  long long twait = 0, tissue = 0;
+  for (int64_t i = pid; i < n_tiles; i += kProducersM) {
     if (i >= S) {
+      const long long tw = SUNSHAPE_CLK();
       mbar_wait(&empty[s], phase ^ 1u, p.err, kErrWaitEmpty);
-      if (ahead > 0) prefetch_next();
+      twait += SUNSHAPE_CLK() - tw;
+      if (ahead > 0 && pid == 0) {
+        prefetch_next();
+        prefetch_next();
+      }
     }
     const int ntok = min(kTileTokens, p.T - t0);
     const int64_t row0 = hh * p.head_stride + t0;
@@ -254,16 +275,29 @@ __device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint6
     }
     __syncwarp();
     if (lane == 0) {
+      const long long ti = SUNSHAPE_CLK();
+#ifdef SUNSHAPE_EXP_BULKV
+      mbar_arrive_expect_tx(&full[s], ntok * DV * 2 + ibulk + hbulk);
+      bulk_g2s(st, reinterpret_cast<const uint8_t*>(p.v) + row0 * DV * 2, ntok * DV * 2, &full[s]);
+#else
       mbar_arrive_expect_tx(&full[s], NBOX * kVBoxBytes + ibulk + hbulk);
 #pragma unroll
       for (int bx = 0; bx < NBOX; ++bx) tma_load_2d(st + bx * kVBoxBytes, &p.tmap_v, bx * 64, (int)row0, &full[s]);
+#endif
       if (ibulk) bulk_g2s(st + p.off_stage_idx, reinterpret_cast<const void*>(ia0), ibulk, &full[s]);
       if (hbulk) bulk_g2s(st + p.off_stage_heavy, reinterpret_cast<const void*>(ha0), hbulk, &full[s]);
+      tissue += SUNSHAPE_CLK() - ti;
     }
     __syncwarp();
-    t0 += kTileTokens;
-    if (t0 >= p.T) { t0 = 0; ++hh; }
-    if (++s == S) { s = 0; phase ^= 1u; }
+    t0 += kProducersM * kTileTokens;
+    while (t0 >= p.tph * kTileTokens) { t0 -= p.tph * kTileTokens; ++hh; }
+    s += kProducersM;
+    while (s >= S) { s -= S; phase ^= 1u; }
+  }
+  if (lane == 0) {
+    SUNSHAPE_TRACE_ADD(0, SUNSHAPE_CLK() - tp0);
+    SUNSHAPE_TRACE_ADD(1, twait);
+    SUNSHAPE_TRACE_ADD(6, tissue);
   }
 }
 
@@ -312,8 +346,8 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   const int n_heavy = flag_s[2];
   if (te <= tb) return;
 
-  if (warp == kWarpsM) {
-    produce_mma<DV>(p, tb, te, full, empty, stage0, n_heavy, lane);
+  if (warp >= kWarpsM) {
+    produce_mma<DV>(p, tb, te, full, empty, stage0, n_heavy, lane, warp - kWarpsM);
     return;
   }
 
@@ -329,12 +363,16 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   const bool fast_idx = (p.nb & 7) == 0;
   const int gid = lane >> 2, tig = lane & 3;
 
+  const long long tc0 = SUNSHAPE_CLK();
+  long long t_wait = 0, t_lut = 0, t_end = 0;
   int64_t f = tb;
   while (f < te) {
     const int64_t hh = f / p.tph;
     const int64_t fend = min(te, (hh + 1) * p.tph);
     const int i0 = (int)(f - tb), i1 = (int)(fend - tb);
+    const long long tl = SUNSHAPE_CLK();
     build_lut_m<GP>(p, hh, perm_s, hslot_s, q_s, lut, ctid);
+    t_lut += SUNSHAPE_CLK() - tl;
 
     float m_run[GP], l_run[GP];
     float acc[MT][NT][4];
@@ -355,7 +393,9 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
     uint32_t phase = (uint32_t)((ifirst / p.stages) & 1);
     const int64_t seg_tile0 = hh * p.tph;
     for (int i = ifirst; i < i1; i += kTileGroupsM) {
+      const long long tw = SUNSHAPE_CLK();
       mbar_wait(&full[s], phase, p.err, kErrWaitFull);
+      t_wait += SUNSHAPE_CLK() - tw;
       const int t0 = (int)(tb + i - seg_tile0) * kTileTokens;
       const int ntok = min(kTileTokens, p.T - t0);
       const int64_t row0 = hh * p.head_stride + t0;
@@ -517,6 +557,7 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
     }
 
     // ---------------- segment end: per-warp partials -> staging -> merge
+    const long long te0 = SUNSHAPE_CLK();
     float l_tot[GP];
 #pragma unroll
     for (int g = 0; g < GP; ++g) l_tot[g] = warp_sum(l_run[g]);
@@ -544,7 +585,14 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
       }
     named_barrier(kBarConsumers, kConsumerThreadsM);
     finish_segment<GP, DV, kWarpsM>(p, stg, hh, tb, grid, ctid, flag_s);
+    t_end += SUNSHAPE_CLK() - te0;
     f = fend;
+  }
+  if (lane == 0) {
+    SUNSHAPE_TRACE_ADD(2, SUNSHAPE_CLK() - tc0);
+    SUNSHAPE_TRACE_ADD(3, t_wait);
+    SUNSHAPE_TRACE_ADD(4, t_lut);
+    SUNSHAPE_TRACE_ADD(5, t_end);
   }
 }
 
