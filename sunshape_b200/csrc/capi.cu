@@ -90,6 +90,7 @@ int num_sms() {
 int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
 struct DecodePlan {
+  bool lut16 = false;   // tensor-core kernel: fp16 (scaled) LUT entries
   int gp = 0;           // padded rows per launch (4, 8 or 16)
   int chunk_rows = 0;   // rows per launch
   int stages = 0;
@@ -174,8 +175,10 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
     return false;
   }
   for (int gp = pick_gp(rows);; gp /= 2) {
+   // fp32 LUT entries first; a half-size fp16 LUT when fp32 would leave fewer than 6 stages
+   for (int l16 = 0; l16 < (gp >= 8 ? 2 : 1); ++l16) {
     const int nt = (gp + 7) / 8;
-    const int lut_bytes = nbh * 8 * kLutC * gp * 4;
+    const int lut_bytes = nbh * 8 * kLutC * gp * (l16 ? 2 : 4);
     const int stg_bytes = kWarpsM * gp * (dv + 2) * 4;
     const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
     const int off_perm = 256;
@@ -189,7 +192,9 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
     const int hpart = n_heavy > 0 ? round_up(kTileTokens * n_heavy * bd * hsize + 32, 128) : 0;
     const int stage_bytes = round_up(vpart + ipart + hpart, 1024);
     const int stages = std::min(kMaxStages, (kSmemLimit - 1024 - off_stage) / stage_bytes);
-    if (stages >= 2) {
+    const bool last = l16 == 1 || gp < 8;
+    if (stages >= 6 || (last && stages >= 2)) {
+      pl.lut16 = l16 == 1;
       pl.gp = gp;
       pl.chunk_rows = std::min(rows, gp);
       pl.stages = stages;
@@ -217,6 +222,7 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
       pl.ws_bytes = 256 + round_up(n_heads * 4, 256) + pl.grid * p.max_seg * gp * (int64_t)(dv + 2) * 4;
       return true;
     }
+   }
     if (gp == 4) break;
   }
   why = "decode configuration does not fit in shared memory (n_blocks, rows).";
@@ -254,7 +260,13 @@ int make_value_map(CUtensorMap* map, const void* v, int dtype, int dv, int64_t r
 template <int GP, int DV, typename VT>
 void run_mma(const DecodePlan& pl, cudaStream_t st) {
   DecodeLaunch l{pl.prm, pl.smem, pl.grid};
-  launch_decode_mma_t<GP, DV, VT>(l, st);
+  if constexpr (GP >= 8) {
+    if (pl.lut16) {
+      launch_decode_mma_t<GP, DV, VT, true>(l, st);
+      return;
+    }
+  }
+  launch_decode_mma_t<GP, DV, VT, false>(l, st);
 }
 
 int launch_decode_mma(const DecodePlan& pl, int dv, int vdt, cudaStream_t st) {

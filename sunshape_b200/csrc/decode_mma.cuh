@@ -107,10 +107,31 @@ __device__ __forceinline__ uint32_t p_chunk_offset(int row, int chunk) {
 
 // LUT rows of one block for this thread: q block held in registers, codebook rows loaded
 // four at a time so their L2 latencies overlap; stores land in bank group b & 7.
-template <int GP, int BD>
+// Store one LUT entry (GP query rows of block b, codeword c): fp32 in GP/4 16-byte halves,
+// or (L16) fp16 scaled by `scale` in GP/8 16-byte halves.
+template <int GP, bool L16>
+__device__ __forceinline__ void store_lut_entry(uint8_t* dst_base, int c, const float (&v)[GP], float scale) {
+  if constexpr (L16) {
+#pragma unroll
+    for (int h = 0; h < GP / 8; ++h) {
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        w[k] = (uint32_t)__half_as_ushort(__float2half_rn(v[8 * h + 2 * k] * scale)) |
+               ((uint32_t)__half_as_ushort(__float2half_rn(v[8 * h + 2 * k + 1] * scale)) << 16);
+      *reinterpret_cast<uint4*>(dst_base + ((int64_t)h * kLutC + c) * 128) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < GP / 4; ++h)
+      *reinterpret_cast<float4*>(dst_base + ((int64_t)h * kLutC + c) * 128) =
+          make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+  }
+}
+
+template <int GP, int BD, bool L16>
 __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float* qblk, const float* cbb, bool active,
-                                             uint8_t* dst_base, int c0) {
-  constexpr int NH = GP / 4;
+                                             uint8_t* dst_base, int c0, float scale) {
   float q[GP][BD];
 #pragma unroll
   for (int g = 0; g < GP; ++g)
@@ -136,10 +157,7 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
         for (int d = 0; d < BD; ++d) a = fmaf(q[g][d], x[u][d], a);
         v[g] = a;
       }
-#pragma unroll
-      for (int h = 0; h < NH; ++h)
-        *reinterpret_cast<float4*>(dst_base + ((int64_t)h * kLutC + c) * 128) =
-            make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+      store_lut_entry<GP, L16>(dst_base, c, v, scale);
     }
   }
 }
@@ -147,11 +165,15 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
 // LUT of flat head hh for the tensor-core kernel: 16-byte entry (b, h, c) at
 // ((kh * NH + h) * 256 + c) * 128 + (b & 7) * 16 with kh = b / 8, holding q rows 4h..4h+3.
 // Heavy and padding blocks get zero rows (their stored index is 0).
-template <int GP>
+// With L16 the entries are stored as fp16 times a power-of-two scale chosen from the bound
+// |q_b . c| <= max_b |q_b| * max_{b,c} |c|, so no entry can overflow; the score is the fp32 sum
+// of the entries times 1 / scale (exact).  The scale is left in *scale_s.
+template <int GP, bool L16>
 __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
-                            float* q_s, uint8_t* lut, int ctid) {
-  constexpr int NH = GP / 4;
+                            float* q_s, uint8_t* lut, int ctid, float* scale_s) {
+  constexpr int NH = L16 ? GP / 8 : GP / 4;
   named_barrier(kBarConsumers, kConsumerThreadsM);
+  if (L16 && ctid == 0) { scale_s[1] = 0.f; scale_s[2] = 0.f; }
   for (int e = ctid; e < GP * p.D; e += kConsumerThreadsM) {
     const int g = e / p.D, dp = e - g * p.D;
     float v = 0.f;
@@ -167,6 +189,34 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
   const int cbh = p.n_cb == 1 ? 0 : (int)((hh % p.kv_heads) % p.n_cb);
   const float* cb = p.cb + (int64_t)cbh * p.nb * p.C * p.bd;
   const int blo = ctid & 7, c0 = ctid >> 3;   // 8 bank groups x 32 codeword lanes
+  float scale = 1.f;
+  if constexpr (L16) {
+    float qn = 0.f, cn = 0.f;
+    for (int e = ctid; e < GP * p.nb; e += kConsumerThreadsM) {
+      const int g = e / p.nb, b = e - g * p.nb;
+      float a = 0.f;
+      for (int d = 0; d < p.bd; ++d) a = fmaf(q_s[g * p.D + b * p.bd + d], q_s[g * p.D + b * p.bd + d], a);
+      qn = fmaxf(qn, a);
+    }
+    for (int e = ctid; e < p.nb * p.C; e += kConsumerThreadsM) {
+      const int b = e / p.C;
+      if (hslot_s[b] >= 0) continue;
+      const float* r = cb + (int64_t)e * p.bd;
+      float a = 0.f;
+      for (int d = 0; d < p.bd; ++d) a = fmaf(__ldg(r + d), __ldg(r + d), a);
+      cn = fmaxf(cn, a);
+    }
+    qn = warp_max(qn);
+    cn = warp_max(cn);
+    if ((ctid & 31) == 0) {
+      atomicMax(reinterpret_cast<int*>(scale_s + 1), __float_as_int(qn));
+      atomicMax(reinterpret_cast<int*>(scale_s + 2), __float_as_int(cn));
+    }
+    named_barrier(kBarConsumers, kConsumerThreadsM);
+    const float bound = sqrtf(scale_s[1]) * sqrtf(scale_s[2]) * 1.001f;
+    scale = bound > 0.f ? exp2f(fminf(100.f, floorf(log2f(32768.f / bound)))) : 1.f;
+    if (ctid == 0) scale_s[0] = 1.f / scale;
+  }
   for (int kh = 0; kh < p.nbh; ++kh) {
     const int b = blo + 8 * kh;
     const bool active = b < p.nb && hslot_s[b] < 0;
@@ -174,9 +224,9 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
     const float* cbb = cb + (int64_t)(active ? b : 0) * p.C * p.bd;
     uint8_t* dst = lut + (int64_t)kh * NH * kLutC * 128 + blo * 16;
     if (p.bd == 8) {
-      lut_rows_reg<GP, 8>(p, qblk, cbb, active, dst, c0);
+      lut_rows_reg<GP, 8, L16>(p, qblk, cbb, active, dst, c0, scale);
     } else if (p.bd == 4) {
-      lut_rows_reg<GP, 4>(p, qblk, cbb, active, dst, c0);
+      lut_rows_reg<GP, 4, L16>(p, qblk, cbb, active, dst, c0, scale);
     } else {
       for (int c = c0; c < p.C; c += 32) {
         float v[GP];
@@ -188,10 +238,7 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
 #pragma unroll
             for (int g = 0; g < GP; ++g) v[g] = fmaf(qblk[g * p.D + d], x, v[g]);
           }
-#pragma unroll
-        for (int h = 0; h < NH; ++h)
-          *reinterpret_cast<float4*>(dst + ((int64_t)h * kLutC + c) * 128) =
-              make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+        store_lut_entry<GP, L16>(dst, c, v, scale);
       }
     }
   }
@@ -301,12 +348,12 @@ __device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint6
   }
 }
 
-template <int GP, int DV, typename VT>
+template <int GP, int DV, typename VT, bool L16>
 __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128B-swizzled TMA boxes need 1024-byte aligned destinations: align the carve-up base
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  constexpr int NH = GP / 4;          // 16-byte LUT halves per (block, codeword)
+  constexpr int NH = L16 ? GP / 8 : GP / 4;   // 16-byte LUT chunks per (block, codeword)
   constexpr int NT = (GP + 7) / 8;    // MMA n-tiles (8 query rows each)
   constexpr int MT = DV / 16;         // MMA m-tiles (16 value columns each)
   using Op = MmaOp<VT>;
@@ -314,6 +361,7 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + kMaxStages;
   int* flag_s = reinterpret_cast<int*>(smem + 128);
+  float* scale_s = reinterpret_cast<float*>(smem + 192);   // LUT scale (inverse), norm bounds
   int* perm_s = reinterpret_cast<int*>(smem + p.off_perm);
   int8_t* hslot_s = reinterpret_cast<int8_t*>(smem + p.off_hslot);
   int8_t* hlist_s = hslot_s + 32;                 // heavy block ids in slot order
@@ -371,7 +419,8 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
     const int64_t fend = min(te, (hh + 1) * p.tph);
     const int i0 = (int)(f - tb), i1 = (int)(fend - tb);
     const long long tl = SUNSHAPE_CLK();
-    build_lut_m<GP>(p, hh, perm_s, hslot_s, q_s, lut, ctid);
+    build_lut_m<GP, L16>(p, hh, perm_s, hslot_s, q_s, lut, ctid, scale_s);
+    const float inv_scale = L16 ? scale_s[0] : 1.f;
     t_lut += SUNSHAPE_CLK() - tl;
 
     float m_run[GP], l_run[GP];
@@ -449,11 +498,26 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
               const uint8_t* e = kbase + c * 128u + (uint32_t)(((kl + lane) & 7) << 4);
 #pragma unroll
               for (int h = 0; h < NH; ++h) {
-                const float4 v = *reinterpret_cast<const float4*>(e + h * kLutC * 128);
-                part[2 * h] = __fadd2_rn(part[2 * h], make_float2(v.x, v.y));
-                part[2 * h + 1] = __fadd2_rn(part[2 * h + 1], make_float2(v.z, v.w));
+                if constexpr (L16) {
+                  const uint4 r = *reinterpret_cast<const uint4*>(e + h * kLutC * 128);
+                  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    float2& a = part[4 * h + k];
+                    asm("add.f32.f16 %0, %1, %2;" : "=f"(a.x) : "h"((unsigned short)(w[k] & 0xffffu)), "f"(a.x));
+                    asm("add.f32.f16 %0, %1, %2;" : "=f"(a.y) : "h"((unsigned short)(w[k] >> 16)), "f"(a.y));
+                  }
+                } else {
+                  const float4 v = *reinterpret_cast<const float4*>(e + h * kLutC * 128);
+                  part[2 * h] = __fadd2_rn(part[2 * h], make_float2(v.x, v.y));
+                  part[2 * h + 1] = __fadd2_rn(part[2 * h + 1], make_float2(v.z, v.w));
+                }
               }
             }
+          }
+          if constexpr (L16) {
+#pragma unroll
+            for (int g = 0; g < GP / 2; ++g) { part[g].x *= inv_scale; part[g].y *= inv_scale; }
           }
           // SunShape-Mixed heavy blocks: dense dot of the stored block with the permuted query
           for (int hs = 0; hs < n_heavy; ++hs) {
@@ -596,32 +660,44 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   }
 }
 
-template <int GP, int DV, typename VT>
+template <int GP, int DV, typename VT, bool L16>
 void launch_decode_mma_t(const DecodeLaunch& l, cudaStream_t st) {
-  auto k = decode_mma_kernel<GP, DV, VT>;
+  auto k = decode_mma_kernel<GP, DV, VT, L16>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem);
   k<<<(unsigned)l.grid, kThreadsM, l.smem, st>>>(l.prm);
 }
 
 
 // Instantiated in decode_mma_bf16.cu / decode_mma_f16.cu.
-extern template void launch_decode_mma_t<4, 64, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<4, 128, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<4, 256, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<8, 64, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<8, 128, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<8, 256, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<16, 64, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<16, 128, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<16, 256, __nv_bfloat16>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<4, 64, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<4, 128, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<4, 256, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<8, 64, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<8, 128, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<8, 256, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<16, 64, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<16, 128, __half>(const DecodeLaunch&, cudaStream_t);
-extern template void launch_decode_mma_t<16, 256, __half>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 256, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 64, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 128, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 256, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 256, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 64, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 128, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 256, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 256, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 64, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 128, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 256, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 64, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 64, __half, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 128, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 128, __half, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 256, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<8, 256, __half, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 64, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 64, __half, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 128, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 128, __half, true>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 256, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<16, 256, __half, true>(const DecodeLaunch&, cudaStream_t);
 
 }  // namespace sunshape
