@@ -126,9 +126,10 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
     const int ipart = round_up(kTileTokens * nb + 32, 128);
     const int hpart = n_heavy_max > 0 ? round_up(kTileTokens * n_heavy_max * bd * hsize + 32, 128) : 0;
     const int stage_bytes = vpart + ipart + hpart;
-    const int stages = std::min(kMaxStages, (kSmemLimit - off_stage) / stage_bytes);
+    // multiple of the consumer tile groups: each stage is drained by one group in tile order
+    const int stages = std::min(kMaxStages, (kSmemLimit - off_stage) / stage_bytes) / kTileGroups * kTileGroups;
     const bool regs_ok = scores_only || gp * (dv / 32) <= 64;
-    if (stages >= 2 && regs_ok) {
+    if (stages >= kTileGroups && regs_ok) {
       pl.gp = gp;
       pl.chunk_rows = std::min(rows, gp);
       pl.stages = stages;
@@ -176,7 +177,9 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
   }
   for (int gp = pick_gp(rows);; gp /= 2) {
    // fp32 LUT entries first; a half-size fp16 LUT when fp32 would leave fewer than 6 stages
-   for (int l16 = 0; l16 < (gp >= 8 ? 2 : 1); ++l16) {
+   // (GP = 4 packs two block groups per 16-byte slot, so it needs an even number of groups)
+   const bool l16_ok = gp >= 8 || (nbh % 2 == 0);
+   for (int l16 = 0; l16 < (l16_ok ? 2 : 1); ++l16) {
     const int nt = (gp + 7) / 8;
     const int lut_bytes = nbh * 8 * kLutC * gp * (l16 ? 2 : 4);
     const int stg_bytes = kWarpsM * gp * (dv + 2) * 4;
@@ -191,9 +194,13 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
     const int ipart = round_up(kTileTokens * nb + 32, 128);
     const int hpart = n_heavy > 0 ? round_up(kTileTokens * n_heavy * bd * hsize + 32, 128) : 0;
     const int stage_bytes = round_up(vpart + ipart + hpart, 1024);
-    const int stages = std::min(kMaxStages, (kSmemLimit - 1024 - off_stage) / stage_bytes);
-    const bool last = l16 == 1 || gp < 8;
-    if (stages >= 6 || (last && stages >= 2)) {
+    // Stage count is a multiple of the consumer tile groups (and of the producer count), so
+    // every stage is filled by one producer warp and drained by one tile group, both in tile
+    // order: a phase-parity wait can then never match an older phase of the same stage.
+    const int stages = std::min(kMaxStages, (kSmemLimit - 1024 - off_stage) / stage_bytes) / kTileGroupsM *
+                       kTileGroupsM;
+    const bool last = l16 == 1 || !l16_ok;
+    if (stages >= 8 || (last && stages >= kTileGroupsM)) {
       pl.lut16 = l16 == 1;
       pl.gp = gp;
       pl.chunk_rows = std::min(rows, gp);
@@ -260,13 +267,8 @@ int make_value_map(CUtensorMap* map, const void* v, int dtype, int dv, int64_t r
 template <int GP, int DV, typename VT>
 void run_mma(const DecodePlan& pl, cudaStream_t st) {
   DecodeLaunch l{pl.prm, pl.smem, pl.grid};
-  if constexpr (GP >= 8) {
-    if (pl.lut16) {
-      launch_decode_mma_t<GP, DV, VT, true>(l, st);
-      return;
-    }
-  }
-  launch_decode_mma_t<GP, DV, VT, false>(l, st);
+  if (pl.lut16) launch_decode_mma_t<GP, DV, VT, true>(l, st);
+  else launch_decode_mma_t<GP, DV, VT, false>(l, st);
 }
 
 int launch_decode_mma(const DecodePlan& pl, int dv, int vdt, cudaStream_t st) {

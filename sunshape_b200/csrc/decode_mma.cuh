@@ -107,11 +107,18 @@ __device__ __forceinline__ uint32_t p_chunk_offset(int row, int chunk) {
 
 // LUT rows of one block for this thread: q block held in registers, codebook rows loaded
 // four at a time so their L2 latencies overlap; stores land in bank group b & 7.
-// Store one LUT entry (GP query rows of block b, codeword c): fp32 in GP/4 16-byte halves,
-// or (L16) fp16 scaled by `scale` in GP/8 16-byte halves.
+// Store one LUT entry (GP query rows of block b, codeword c): fp32 in GP/4 16-byte chunks,
+// or (L16) fp16 scaled by `scale` in GP/8 16-byte chunks -- for GP == 4 an 8-byte half of a
+// 16-byte slot shared by block groups kh = 2j and 2j + 1 (dst_base already points at the half).
 template <int GP, bool L16>
 __device__ __forceinline__ void store_lut_entry(uint8_t* dst_base, int c, const float (&v)[GP], float scale) {
-  if constexpr (L16) {
+  if constexpr (L16 && GP == 4) {
+    const uint32_t w0 = (uint32_t)__half_as_ushort(__float2half_rn(v[0] * scale)) |
+                        ((uint32_t)__half_as_ushort(__float2half_rn(v[1] * scale)) << 16);
+    const uint32_t w1 = (uint32_t)__half_as_ushort(__float2half_rn(v[2] * scale)) |
+                        ((uint32_t)__half_as_ushort(__float2half_rn(v[3] * scale)) << 16);
+    *reinterpret_cast<uint2*>(dst_base + (int64_t)c * 128) = make_uint2(w0, w1);
+  } else if constexpr (L16) {
 #pragma unroll
     for (int h = 0; h < GP / 8; ++h) {
       uint32_t w[4];
@@ -171,7 +178,7 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
 template <int GP, bool L16>
 __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
                             float* q_s, uint8_t* lut, int ctid, float* scale_s) {
-  constexpr int NH = L16 ? GP / 8 : GP / 4;
+  constexpr int NH = L16 ? (GP >= 8 ? GP / 8 : 1) : GP / 4;
   named_barrier(kBarConsumers, kConsumerThreadsM);
   if (L16 && ctid == 0) { scale_s[1] = 0.f; scale_s[2] = 0.f; }
   for (int e = ctid; e < GP * p.D; e += kConsumerThreadsM) {
@@ -222,7 +229,8 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
     const bool active = b < p.nb && hslot_s[b] < 0;
     const float* qblk = q_s + (active ? b : 0) * p.bd;
     const float* cbb = cb + (int64_t)(active ? b : 0) * p.C * p.bd;
-    uint8_t* dst = lut + (int64_t)kh * NH * kLutC * 128 + blo * 16;
+    uint8_t* dst = (L16 && GP == 4) ? lut + (int64_t)(kh >> 1) * kLutC * 128 + blo * 16 + (kh & 1) * 8
+                                    : lut + (int64_t)kh * NH * kLutC * 128 + blo * 16;
     if (p.bd == 8) {
       lut_rows_reg<GP, 8, L16>(p, qblk, cbb, active, dst, c0, scale);
     } else if (p.bd == 4) {
@@ -353,7 +361,7 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128B-swizzled TMA boxes need 1024-byte aligned destinations: align the carve-up base
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  constexpr int NH = L16 ? GP / 8 : GP / 4;   // 16-byte LUT chunks per (block, codeword)
+  constexpr int NH = L16 ? (GP >= 8 ? GP / 8 : 1) : GP / 4;   // 16-byte LUT chunks per (block, codeword)
   constexpr int NT = (GP + 7) / 8;    // MMA n-tiles (8 query rows each)
   constexpr int MT = DV / 16;         // MMA m-tiles (16 value columns each)
   using Op = MmaOp<VT>;
@@ -475,9 +483,13 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
         if (valid) {
           const uint8_t* irow = itile + t * p.nb;
           const int rot = lane & 7;
+          // GP == 4 fp16 LUT: lanes 8-15 of each 16-lane phase walk each block-group pair in the
+          // opposite order, so the two 8-byte halves of a slot are read by different lanes
+          const int kswap = (L16 && GP == 4) ? ((lane >> 3) & 1) : 0;
 #pragma unroll
-          for (int kh = 0; kh < 4; ++kh) {
-            if (kh >= p.nbh) break;
+          for (int kk = 0; kk < 4; ++kk) {
+            if (kk >= p.nbh) break;
+            const int kh = kk ^ kswap;
             uint64_t w;
             if (fast_idx) {
               w = *reinterpret_cast<const uint64_t*>(irow + 8 * kh);
@@ -491,11 +503,20 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
             // rotate so byte kl of w holds block 8*kh + ((kl + lane) & 7)
             const uint64_t wr = rot ? ((w >> (8 * rot)) | (w << (64 - 8 * rot))) : w;
             const uint32_t lo = (uint32_t)wr, hi = (uint32_t)(wr >> 32);
-            const uint8_t* kbase = lut + kh * NH * kLutC * 128;
+            const uint8_t* kbase = (L16 && GP == 4) ? lut + (kh >> 1) * kLutC * 128 + (kh & 1) * 8
+                                                    : lut + kh * NH * kLutC * 128;
 #pragma unroll
             for (int kl = 0; kl < 8; ++kl) {
               const uint32_t c = ((kl < 4 ? lo : hi) >> (8 * (kl & 3))) & 0xffu;
               const uint8_t* e = kbase + c * 128u + (uint32_t)(((kl + lane) & 7) << 4);
+              if constexpr (L16 && GP == 4) {
+                const uint2 r = *reinterpret_cast<const uint2*>(e);
+                asm("add.f32.f16 %0, %1, %2;" : "=f"(part[0].x) : "h"((unsigned short)(r.x & 0xffffu)), "f"(part[0].x));
+                asm("add.f32.f16 %0, %1, %2;" : "=f"(part[0].y) : "h"((unsigned short)(r.x >> 16)), "f"(part[0].y));
+                asm("add.f32.f16 %0, %1, %2;" : "=f"(part[1].x) : "h"((unsigned short)(r.y & 0xffffu)), "f"(part[1].x));
+                asm("add.f32.f16 %0, %1, %2;" : "=f"(part[1].y) : "h"((unsigned short)(r.y >> 16)), "f"(part[1].y));
+                continue;
+              }
 #pragma unroll
               for (int h = 0; h < NH; ++h) {
                 if constexpr (L16) {
@@ -520,6 +541,30 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
             for (int g = 0; g < GP / 2; ++g) { part[g].x *= inv_scale; part[g].y *= inv_scale; }
           }
           // SunShape-Mixed heavy blocks: dense dot of the stored block with the permuted query
+          if (n_heavy > 0 && p.bd == 8 && hsize == 2 && (reinterpret_cast<uintptr_t>(htile) & 15) == 0) {
+            // bf16 blocks of 8: one 16-byte load of the stored block, query rows as float4 pairs
+            for (int hs = 0; hs < n_heavy; ++hs) {
+              const int b = hlist_s[hs];
+              const uint4 raw = *reinterpret_cast<const uint4*>(htile + ((int64_t)t * n_heavy + hs) * 16);
+              const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+              float x[8];
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                x[2 * k] = __uint_as_float(rw[k] << 16);
+                x[2 * k + 1] = __uint_as_float(rw[k] & 0xffff0000u);
+              }
+              const float* qb = q_s + b * 8;
+#pragma unroll
+              for (int g = 0; g < GP; ++g) {
+                const float4 q0 = *reinterpret_cast<const float4*>(qb + g * p.D);
+                const float4 q1 = *reinterpret_cast<const float4*>(qb + g * p.D + 4);
+                float a = (g & 1) ? part[g >> 1].y : part[g >> 1].x;
+                a = fmaf(q0.x, x[0], a); a = fmaf(q0.y, x[1], a); a = fmaf(q0.z, x[2], a); a = fmaf(q0.w, x[3], a);
+                a = fmaf(q1.x, x[4], a); a = fmaf(q1.y, x[5], a); a = fmaf(q1.z, x[6], a); a = fmaf(q1.w, x[7], a);
+                if (g & 1) part[g >> 1].y = a; else part[g >> 1].x = a;
+              }
+            }
+          } else
           for (int hs = 0; hs < n_heavy; ++hs) {
             const int b = hlist_s[hs];
             const uint8_t* hv = htile + ((int64_t)t * n_heavy + hs) * p.bd * hsize;
@@ -670,8 +715,11 @@ void launch_decode_mma_t(const DecodeLaunch& l, cudaStream_t st) {
 
 // Instantiated in decode_mma_bf16.cu / decode_mma_f16.cu.
 extern template void launch_decode_mma_t<4, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 64, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<4, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 128, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<4, 256, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 256, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<8, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<8, 64, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<8, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
@@ -685,8 +733,11 @@ extern template void launch_decode_mma_t<16, 128, __nv_bfloat16, true>(const Dec
 extern template void launch_decode_mma_t<16, 256, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<16, 256, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<4, 64, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 64, __half, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<4, 128, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 128, __half, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<4, 256, __half, false>(const DecodeLaunch&, cudaStream_t);
+extern template void launch_decode_mma_t<4, 256, __half, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<8, 64, __half, false>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<8, 64, __half, true>(const DecodeLaunch&, cudaStream_t);
 extern template void launch_decode_mma_t<8, 128, __half, false>(const DecodeLaunch&, cudaStream_t);

@@ -2,8 +2,11 @@
 #include "decode_mma.cuh"
 namespace sunshape {
 template void launch_decode_mma_t<4, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+template void launch_decode_mma_t<4, 64, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 template void launch_decode_mma_t<4, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+template void launch_decode_mma_t<4, 128, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 template void launch_decode_mma_t<4, 256, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
+template void launch_decode_mma_t<4, 256, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 template void launch_decode_mma_t<8, 64, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
 template void launch_decode_mma_t<8, 64, __nv_bfloat16, true>(const DecodeLaunch&, cudaStream_t);
 template void launch_decode_mma_t<8, 128, __nv_bfloat16, false>(const DecodeLaunch&, cudaStream_t);
