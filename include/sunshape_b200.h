@@ -61,6 +61,8 @@ typedef struct sunshape_codec {
   int32_t block_dim;
   int32_t n_centroids;
   int32_t n_heavy;             /* number of nonzero heavy_mask entries (0 without a mask)  */
+  const float* centroid_norm_max; /* [n_cb] max_{b,c} |centroids[cb,b,c,:]| (optional, NULL =
+                                     computed on the device when a kernel needs it)            */
 } sunshape_codec_t;
 
 /* Quantized KV storage of n_heads (= batch * kv_heads) heads, head-major.

@@ -41,6 +41,7 @@ class CodecDesc(ctypes.Structure):
         ("block_dim", ctypes.c_int32),
         ("n_centroids", ctypes.c_int32),
         ("n_heavy", ctypes.c_int32),
+        ("centroid_norm_max", ctypes.c_void_p),
     ]
 
 
@@ -141,10 +142,11 @@ def stream_ptr(dev: torch.device) -> int:
 
 
 def codec_desc(centroids: torch.Tensor, perm: torch.Tensor, heavy_mask: torch.Tensor | None,
-               n_heavy: int, head_dim: int, block_dim: int) -> CodecDesc:
-    """centroids [n_cb, nb, C, bd] fp32 contiguous, perm int64 [D], heavy_mask uint8 [nb] or None."""
+               n_heavy: int, head_dim: int, block_dim: int, norm_max: torch.Tensor | None = None) -> CodecDesc:
+    """centroids [n_cb, nb, C, bd] fp32 contiguous, perm int64 [D], heavy_mask uint8 [nb] or None,
+    norm_max [n_cb] fp32 (max centroid norm per codebook) or None."""
     return CodecDesc(ptr(centroids), ptr(perm), ptr(heavy_mask), int(centroids.shape[0]), int(head_dim),
-                     int(block_dim), int(centroids.shape[2]), int(n_heavy))
+                     int(block_dim), int(centroids.shape[2]), int(n_heavy), ptr(norm_max))
 
 
 def kv_desc(indices: torch.Tensor, heavy: torch.Tensor | None, value: torch.Tensor | None, seq_len: int,

@@ -145,8 +145,10 @@ class SunShapeBlockCodec(torch.nn.Module):
             n_heavy = int(hm.sum().item())
             if n_heavy:
                 heavy = hm.to(torch.uint8).contiguous()
-        desc = _lib.codec_desc(cents, perm, heavy, n_heavy, self.head_dim, self.block_dim)
-        dc = (desc, (cents, perm, heavy), n_heavy)
+        # largest centroid norm per codebook: bounds |q_b . c| for the fp16 LUT scale
+        norm_max = cents.norm(dim=-1).amax(dim=(1, 2)).contiguous()
+        desc = _lib.codec_desc(cents, perm, heavy, n_heavy, self.head_dim, self.block_dim, norm_max)
+        dc = (desc, (cents, perm, heavy, norm_max), n_heavy)
         self._desc_cache = dc
         return dc
 

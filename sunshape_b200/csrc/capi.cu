@@ -421,6 +421,7 @@ int sunshape_dequantize(const sunshape_codec_t* codec, const sunshape_kv_t* kv, 
 static int fill_common(DecodeParams& p, const sunshape_codec_t* codec, const sunshape_kv_t* kv, int n_heads,
                        int kv_heads) {
   p.cb = codec->centroids; p.n_cb = codec->n_cb; p.perm = codec->permutation; p.heavy_mask = codec->heavy_mask;
+  p.cb_norm_max = codec->centroid_norm_max;
   p.D = codec->head_dim; p.bd = codec->block_dim; p.nb = p.D / p.bd; p.C = codec->n_centroids;
   p.nbh = (p.nb + 7) / 8;
   p.idx = reinterpret_cast<const uint8_t*>(kv->indices);

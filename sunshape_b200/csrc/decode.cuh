@@ -58,6 +58,7 @@ struct DecodeParams {
   int kv_heads;
   // codec
   const float* cb;
+  const float* cb_norm_max;   // [n_cb] or nullptr
   int n_cb;
   const int64_t* perm;
   const uint8_t* heavy_mask;

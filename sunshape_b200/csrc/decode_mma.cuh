@@ -149,8 +149,13 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int c = cb4 + 32 * u;
+      const bool ok = active && c < p.C;
 #pragma unroll
-      for (int d = 0; d < BD; ++d) x[u][d] = (active && c < p.C) ? __ldg(cbb + (int64_t)c * BD + d) : 0.f;
+      for (int d4 = 0; d4 < BD; d4 += 4) {   // codebook rows are 16-byte aligned (BD = 4 or 8)
+        const float4 v = ok ? __ldg(reinterpret_cast<const float4*>(cbb + (int64_t)c * BD + d4))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[u][d4] = v.x; x[u][d4 + 1] = v.y; x[u][d4 + 2] = v.z; x[u][d4 + 3] = v.w;
+      }
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -205,13 +210,18 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
       for (int d = 0; d < p.bd; ++d) a = fmaf(q_s[g * p.D + b * p.bd + d], q_s[g * p.D + b * p.bd + d], a);
       qn = fmaxf(qn, a);
     }
-    for (int e = ctid; e < p.nb * p.C; e += kConsumerThreadsM) {
-      const int b = e / p.C;
-      if (hslot_s[b] >= 0) continue;
-      const float* r = cb + (int64_t)e * p.bd;
-      float a = 0.f;
-      for (int d = 0; d < p.bd; ++d) a = fmaf(__ldg(r + d), __ldg(r + d), a);
-      cn = fmaxf(cn, a);
+    if (p.cb_norm_max != nullptr) {
+      const float m = __ldg(p.cb_norm_max + cbh);
+      cn = m * m;
+    } else {
+      for (int e = ctid; e < p.nb * p.C; e += kConsumerThreadsM) {
+        const int b = e / p.C;
+        if (hslot_s[b] >= 0) continue;
+        const float* r = cb + (int64_t)e * p.bd;
+        float a = 0.f;
+        for (int d = 0; d < p.bd; ++d) a = fmaf(__ldg(r + d), __ldg(r + d), a);
+        cn = fmaxf(cn, a);
+      }
     }
     qn = warp_max(qn);
     cn = warp_max(cn);

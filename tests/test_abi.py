@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header():
     # pointer fields then int32 fields; the header order is mirrored by the ctypes structs
-    assert ctypes.sizeof(_lib.CodecDesc) == 3 * 8 + 5 * 4 + 4  # padded to 8
+    assert ctypes.sizeof(_lib.CodecDesc) == 3 * 8 + 5 * 4 + 4 + 8  # padded to 8
     assert ctypes.sizeof(_lib.KVDesc) == 8 + 4 + 4 + 8 + 4 + 4 + 8 + 4 + 4 + 4 + 4 + 8
 
 
@@ -42,19 +42,19 @@ def _expect(rc, code, text):
 def test_invalid_arguments_are_rejected_before_any_launch():
     lib = _lib.load_library()
     _expect(lib.sunshape_encode(None, None, 0, 1, 1, 1, 0, 0, None, 3, None, 1, 1, None), -1, "codec descriptor")
-    cd = _lib.CodecDesc(16, 16, None, 1, 64, 7, 256, 0)       # head_dim not divisible by block_dim
+    cd = _lib.CodecDesc(16, 16, None, 1, 64, 7, 256, 0, None)       # head_dim not divisible by block_dim
     _expect(lib.sunshape_encode(ctypes.byref(cd), 16, 0, 1, 1, 1, 0, 0, 16, 3, None, 1, 1, None), -1,
             "divisible by block_dim")
-    cd = _lib.CodecDesc(16, 16, None, 1, 64, 8, 300, 0)       # uint8 too narrow for 300 codewords
+    cd = _lib.CodecDesc(16, 16, None, 1, 64, 8, 300, 0, None)       # uint8 too narrow for 300 codewords
     _expect(lib.sunshape_encode(ctypes.byref(cd), 16, 0, 1, 1, 1, 0, 0, 16, 3, None, 1, 1, None), -1,
             "too narrow")
-    cd = _lib.CodecDesc(16, 16, None, 1, 64, 8, 256, 0)
+    cd = _lib.CodecDesc(16, 16, None, 1, 64, 8, 256, 0, None)
     kd = _lib.KVDesc(16, 3, None, 1, 16, 1, 64, 10, 10)
     # query heads not divisible by kv heads
     _expect(lib.sunshape_decode_attention(ctypes.byref(cd), ctypes.byref(kd), 16, 1, 1, 6, 4, 1, None, 0, 0, 0, 0,
                                           float("nan"), 16, 1, None, 16, 1 << 20, None), -1, "divisible by kv-head")
     # more than 32 blocks is outside the fused LUT kernel
-    cd2 = _lib.CodecDesc(16, 16, None, 1, 128, 2, 256, 0)
+    cd2 = _lib.CodecDesc(16, 16, None, 1, 128, 2, 256, 0, None)
     _expect(lib.sunshape_decode_attention(ctypes.byref(cd2), ctypes.byref(kd), 16, 1, 1, 4, 4, 1, None, 0, 0, 0, 0,
                                           float("nan"), 16, 1, None, 16, 1 << 20, None), -2, "n_blocks > 32")
     # misaligned value buffer
