@@ -130,6 +130,30 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
                               float scale, void* out, int32_t out_dtype, float* partials,
                               void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Size of the scratch array built into the library for sunshape_decode_attention_noalloc. */
+#define SUNSHAPE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
+
+/* sunshape_decode_attention without a workspace and without any device allocation.
+ * No counterpart in the reference: it exists for callers that cannot allocate device memory or
+ * pass a workspace -- plugin hosts whose GPU memory belongs to another allocator, engines that
+ * reserve all device memory up front and forbid allocation while decoding, and bindings with no
+ * CUDA allocator of their own.  Arguments and results are those of sunshape_decode_attention;
+ * the scratch is a fixed array of SUNSHAPE_NOALLOC_SCRATCH_BYTES compiled into the library (each
+ * GPU that loads it keeps that much until the process exits).  Decodes whose workspace
+ * (sunshape_decode_workspace_bytes) exceeds it are rejected with SUNSHAPE_E_WORKSPACE.
+ * The first call on a device looks up the array's device address (with that device current), so
+ * make that first call before any stream capture.  Every call clears the parts of the array that
+ * must start at zero, on the given stream; all calls share the one array, so calls that can
+ * overlap on the GPU (different streams, or different host threads) race and must be serialised
+ * by the caller. */
+int sunshape_decode_attention_noalloc(const sunshape_codec_t* codec, const sunshape_kv_t* kv,
+                                      const void* query, int32_t query_dtype,
+                                      int32_t batch, int32_t q_heads, int32_t kv_heads,
+                                      int32_t query_len, const void* mask, int32_t mask_dtype,
+                                      int64_t mask_sb, int64_t mask_sh, int64_t mask_sq,
+                                      float scale, void* out, int32_t out_dtype, float* partials,
+                                      void* stream);
+
 /* Merge n_parts partial sets [n_parts, rows, 2 + value_dim] (as written by
  * sunshape_decode_attention) into out [rows, value_dim] of out_dtype:
  * M = max m_p, L = sum l_p e^(m_p - M), out = sum acc_p e^(m_p - M) / L. */

@@ -27,7 +27,7 @@ _DTYPE_CODE = {
 EXPORTED_SYMBOLS = (
     "sunshape_abi_version", "sunshape_last_error", "sunshape_encode", "sunshape_dequantize",
     "sunshape_attention_scores", "sunshape_decode_workspace_bytes", "sunshape_decode_attention",
-    "sunshape_merge_partials",
+    "sunshape_merge_partials", "sunshape_decode_attention_noalloc",
 )
 
 
@@ -86,6 +86,9 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sunshape_decode_attention.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64, i64,
                                                   f32, vp, i32, vp, vp, i64, vp]
         lib.sunshape_merge_partials.argtypes = [vp, i32, i64, i32, vp, i32, vp]
+        lib.sunshape_decode_attention_noalloc.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64,
+                                                          i64, f32, vp, i32, vp, vp]
+        lib.sunshape_decode_attention_noalloc.restype = ctypes.c_int
         for name in ("sunshape_encode", "sunshape_dequantize", "sunshape_attention_scores",
                      "sunshape_decode_attention", "sunshape_merge_partials"):
             getattr(lib, name).restype = ctypes.c_int

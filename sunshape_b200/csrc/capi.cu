@@ -344,6 +344,11 @@ int check_kv(const sunshape_kv_t* kv, const sunshape_codec_t* c, bool need_value
 
 }  // namespace
 
+namespace sunshape {
+// lets other translation units of the library report errors through sunshape_last_error()
+int set_last_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace sunshape
+
 extern "C" {
 
 int sunshape_abi_version(void) { return SUNSHAPE_ABI_VERSION; }
