@@ -37,9 +37,10 @@ def shard_mask(attn_mask: torch.Tensor | None, start: int, end: int) -> torch.Te
 def gather_partials(partials: torch.Tensor, group=None) -> torch.Tensor:
     """All-gather [rows, 2 + Dv] fp32 partials into [world, rows, 2 + Dv] (the only collective)."""
     world = dist.get_world_size(group)
-    out = torch.empty((world, *partials.shape), dtype=partials.dtype, device=partials.device)
-    dist.all_gather_into_tensor(out, partials.contiguous(), group=group)
-    return out
+    out = torch.empty((world * partials.shape[0], *partials.shape[1:]), dtype=partials.dtype,
+                      device=partials.device)
+    dist.all_gather_into_tensor(out, partials.contiguous(), group=group)   # concatenated form (NCCL and gloo)
+    return out.view(world, *partials.shape)
 
 
 def merge_gathered(gathered: torch.Tensor, out_shape, out_dtype) -> torch.Tensor:
