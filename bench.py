@@ -219,6 +219,40 @@ def time_steps(fn, steps: int, warmup: int, stream: torch.cuda.Stream, extra_eve
     return start.elapsed_time(end)
 
 
+class GraphStep:
+    """A step captured as a CUDA graph of `per_graph` consecutive steps (every launch of every step is
+    replayed: nothing is cached between steps).  Removes the host launch overhead from the device-side
+    timing; falls back to eager calls if capture is not possible."""
+
+    def __init__(self, fn, per_graph: int = 10):
+        self.fn, self.per_graph, self.graph = fn, per_graph, None
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    fn()
+            torch.cuda.current_stream().wait_stream(s)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(per_graph):
+                    fn()
+            torch.cuda.synchronize()
+            self.graph = g
+        except Exception as exc:   # pragma: no cover - depends on the runtime
+            print(f"[bench] CUDA graph capture unavailable ({exc!r}); timing eager calls", file=sys.stderr)
+            torch.cuda.synchronize()
+
+    def run(self, steps: int):
+        if self.graph is None:
+            for _ in range(steps):
+                self.fn()
+            return steps
+        for _ in range(max(1, steps // self.per_graph)):
+            self.graph.replay()
+        return max(1, steps // self.per_graph) * self.per_graph
+
+
 def run_ours(args, cfg: DecodeConfig):
     from sunshape_b200 import vllm_attn_backend as vab
     from sunshape_b200.distributed import KVShardedDecode
@@ -228,6 +262,8 @@ def run_ours(args, cfg: DecodeConfig):
     torch.cuda.set_device(dev)
     if world > 1:
         import torch.distributed as dist
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"      # keep stdout to the one JSON line
         dist.init_process_group("nccl", device_id=dev)
     codec, idx, heavy, value, query, scale, Tl = build_shard(cfg, rank, world, dev)
     keys = vab.SunShapeQuantizedKeys((), cfg.batch, cfg.kv_heads, Tl, indices=idx, heavy=heavy,
@@ -241,11 +277,11 @@ def run_ours(args, cfg: DecodeConfig):
         def step():
             vab._apply_quantized_attention(codec=codec, query=query, key=keys, value=value, attn_mask=None,
                                            scale=scale, out=out)
-        launches_per_step = 1
+        launches_per_step = 2   # lut_kernel + decode_mma_kernel
     else:
         def step():
             sharded(query, keys, value, scale=scale)
-        launches_per_step = 2
+        launches_per_step = 3   # lut_kernel + decode_mma_kernel + merge (NCCL all-gather not counted)
 
     # decode kernel alone (events around the launch on its stream) for the roofline
     def kernel_only():
@@ -263,14 +299,28 @@ def run_ours(args, cfg: DecodeConfig):
 
     for _ in range(max(3, args.warmup)):
         step()
-    kernel_ms = time_steps(kernel_only, max(20, args.steps // 4), 3, stream) / max(20, args.steps // 4)
+    g_kernel = GraphStep(kernel_only)
+    g_step = GraphStep(step)
+    for _ in range(max(3, args.warmup)):
+        g_step.run(g_step.per_graph)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    nk = g_kernel.run(max(20, args.steps // 4))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    kernel_ms = e0.elapsed_time(e1) / nk
 
     sampler = ClockSampler(local)
     barrier()
     sampler.start()
     time.sleep(0.3)           # let the sampler attach before the timed region
     barrier()
-    t_ms = time_steps(step, args.steps, 0, stream)
+    e0.record(stream)
+    n_steps = g_step.run(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1) * args.steps / n_steps
     barrier()
     # e2e through the public API: pinned host query in, host output out, every step
     from sunshape_b200.integration.vllm import SunShapeVLLMRuntimeState
@@ -335,6 +385,7 @@ def run_ours(args, cfg: DecodeConfig):
                 "d2h_bytes_per_step": out.numel() * out.element_size()},
         "clocks": clocks,
         "gpu_launches": args.steps * launches_per_step,
+        "timing": "device-side: CUDA-graph replay of whole steps (all launches of every step); e2e: eager public-API calls",
     }
     return res, rank, world
 

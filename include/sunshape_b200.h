@@ -111,7 +111,7 @@ int sunshape_attention_scores(const sunshape_codec_t* codec, const sunshape_kv_t
  * counters at zero again, so one workspace serves any number of calls issued in
  * stream order (calls that overlap on the GPU need separate workspaces). */
 int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_t rows,
-                                        int32_t value_dim);
+                                        int32_t value_dim, int32_t n_blocks);
 
 /* Fused quantized-key decode attention (LUT build + LUT-gather scores + online
  * softmax . V, split over the KV sequence inside the GPU).

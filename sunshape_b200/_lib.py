@@ -81,7 +81,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sunshape_encode.argtypes = [pc, vp, i32, i32, i32, i32, i64, i64, vp, i32, vp, i32, i64, vp]
         lib.sunshape_dequantize.argtypes = [pc, pk, i32, i32, vp, vp]
         lib.sunshape_attention_scores.argtypes = [pc, pk, vp, i32, i32, i32, i32, f32, vp, vp]
-        lib.sunshape_decode_workspace_bytes.argtypes = [i32, i32, i32, i32]
+        lib.sunshape_decode_workspace_bytes.argtypes = [i32, i32, i32, i32, i32]
         lib.sunshape_decode_workspace_bytes.restype = ctypes.c_int64
         lib.sunshape_decode_attention.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64, i64,
                                                   f32, vp, i32, vp, vp, i64, vp]
@@ -190,9 +190,10 @@ def attention_scores(cd: CodecDesc, kd: KVDesc, query: torch.Tensor, n_heads: in
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
-def decode_workspace(dev: torch.device, n_heads: int, seq_len: int, rows: int, value_dim: int) -> torch.Tensor:
-    """Zero-initialised workspace cached per (device, stream); the kernels leave it zeroed."""
-    need = int(load_library().sunshape_decode_workspace_bytes(n_heads, seq_len, rows, value_dim))
+def decode_workspace(dev: torch.device, n_heads: int, seq_len: int, rows: int, value_dim: int,
+                     n_blocks: int) -> torch.Tensor:
+    """Zero-initialised workspace cached per (device, stream); the kernels leave the tickets zeroed."""
+    need = int(load_library().sunshape_decode_workspace_bytes(n_heads, seq_len, rows, value_dim, n_blocks))
     key = (dev.index if dev.index is not None else torch.cuda.current_device(), stream_ptr(dev))
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < need:
@@ -217,7 +218,7 @@ def decode_attention(cd: CodecDesc, kd: KVDesc, query: torch.Tensor, batch: int,
     with torch.cuda.device(dev):
         if workspace is None:
             workspace = decode_workspace(dev, batch * kv_heads, kd.seq_len, (q_heads // kv_heads) * query_len,
-                                         kd.value_dim)
+                                         kd.value_dim, cd.head_dim // cd.block_dim)
         _check(lib.sunshape_decode_attention(
             ctypes.byref(cd), ctypes.byref(kd), ptr(query), dtype_code(query), batch, q_heads, kv_heads, query_len,
             ptr(mask), dtype_code(mask) if mask is not None else F32, *mask_strides,

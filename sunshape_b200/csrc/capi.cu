@@ -114,7 +114,8 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
   }
   for (;;) {
     const int lut_bytes = nbh * 8 * C * gp * 4;
-    const int stg_bytes = scores_only ? 0 : kWarps * gp * (dv + 2) * 4;
+    // staging for the warp partials + the contributing-slot table of the cross-CTA merge
+    const int stg_bytes = scores_only ? 0 : kWarps * gp * (dv + 2) * 4 + 16 + 8 * num_sms();
     const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
     const int off_perm = 256;
     const int off_hslot = off_perm + round_up(D * 4, 16);
@@ -145,6 +146,7 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
       p.off_p = off_p;
       p.off_lut = off_lut;
       p.off_stage = off_stage;
+      p.merge_smem_bytes = region;
       const int tph = (T + kTileTokens - 1) / kTileTokens;
       const int64_t total = (int64_t)n_heads * tph;
       pl.grid = std::min<int64_t>(num_sms(), total);
@@ -161,6 +163,29 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
   }
   why = "decode configuration does not fit in shared memory / registers (n_blocks, n_centroids, rows).";
   return false;
+}
+
+// Workspace of the decode kernels: [error word | per-head tickets |
+// per-CTA partial slots | per-head LUTs | per-head LUT scales]; the LUT area is empty when the
+// LUTs are built inside each CTA instead.
+struct MmaWsOffsets { int64_t counters, slots, luts, scales, total; };
+constexpr int64_t kGlobalLutMaxBytes = 48ll << 20;   // per-head LUTs (built by lut_kernel) kept in the workspace up to 48 MiB
+MmaWsOffsets mma_workspace_offsets(int64_t n_heads, int64_t grid, int64_t max_seg, int64_t gp, int64_t dv,
+                                   int64_t lut_bytes) {
+  MmaWsOffsets o;
+  o.counters = 256;
+  o.slots = o.counters + (n_heads * 4 + 255) / 256 * 256;
+  o.luts = o.slots + (grid * max_seg * gp * (dv + 2) * 4 + 255) / 256 * 256;
+  o.scales = o.luts + n_heads * lut_bytes;
+  o.total = o.scales + (n_heads * 4 + 255) / 256 * 256;
+#ifdef SUNSHAPE_TRACE
+  o.total += 4096 * 256;   // per-CTA trace marks
+#endif
+  return o;
+}
+int64_t mma_workspace_bytes(int64_t n_heads, int64_t grid, int64_t max_seg, int64_t gp, int64_t dv,
+                            int64_t lut_bytes) {
+  return mma_workspace_offsets(n_heads, grid, max_seg, gp, dv, lut_bytes).total;
 }
 
 // Shared-memory carve-up and split for the tensor-core kernel (16-bit values).
@@ -182,7 +207,7 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
    for (int l16 = 0; l16 < (l16_ok ? 2 : 1); ++l16) {
     const int nt = (gp + 7) / 8;
     const int lut_bytes = nbh * 8 * kLutC * gp * (l16 ? 2 : 4);
-    const int stg_bytes = kWarpsM * gp * (dv + 2) * 4;
+    const int stg_bytes = kWarpsM * gp * (dv + 2) * 4 + 16 + 8 * num_sms();
     const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
     const int off_perm = 256;
     const int off_hslot = off_perm + round_up(D * 4, 16);
@@ -226,7 +251,9 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
       p.tph = tph;
       p.total_tiles = total;
       p.max_seg = (int)((per_cta + tph - 1) / tph + 1);
-      pl.ws_bytes = 256 + round_up(n_heads * 4, 256) + pl.grid * p.max_seg * gp * (int64_t)(dv + 2) * 4;
+      p.lut_bytes = lut_bytes;
+      p.merge_smem_bytes = off_stage - off_lut;
+      pl.ws_bytes = mma_workspace_bytes(n_heads, pl.grid, p.max_seg, gp, dv, 0);
       return true;
     }
    }
@@ -269,6 +296,18 @@ void run_mma(const DecodePlan& pl, cudaStream_t st) {
   DecodeLaunch l{pl.prm, pl.smem, pl.grid};
   if (pl.lut16) launch_decode_mma_t<GP, DV, VT, true>(l, st);
   else launch_decode_mma_t<GP, DV, VT, false>(l, st);
+}
+
+int launch_lut(const DecodeParams& p, int gp, bool lut16, int n_heads, cudaStream_t st) {
+  switch (gp * 2 + (lut16 ? 1 : 0)) {
+    case 8: launch_lut_t<4, false>(p, n_heads, st); break;
+    case 9: launch_lut_t<4, true>(p, n_heads, st); break;
+    case 16: launch_lut_t<8, false>(p, n_heads, st); break;
+    case 17: launch_lut_t<8, true>(p, n_heads, st); break;
+    case 32: launch_lut_t<16, false>(p, n_heads, st); break;
+    default: launch_lut_t<16, true>(p, n_heads, st); break;
+  }
+  return SUNSHAPE_OK;
 }
 
 int launch_decode_mma(const DecodePlan& pl, int dv, int vdt, cudaStream_t st) {
@@ -477,7 +516,8 @@ int sunshape_attention_scores(const sunshape_codec_t* codec, const sunshape_kv_t
   return cuda_status("scores launch");
 }
 
-int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_t rows, int32_t value_dim) {
+int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_t rows, int32_t value_dim,
+                                        int32_t n_blocks) {
   if (n_heads <= 0 || seq_len <= 0 || rows <= 0) return 256;
   // the slot area depends only on the grid, the split and (gp, value_dim): use the largest gp
   const int gp = pick_gp(rows);
@@ -486,7 +526,10 @@ int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_
   const int64_t grid = std::min<int64_t>(num_sms(), total);
   const int64_t per_cta = (total + grid - 1) / grid;
   const int64_t max_seg = (per_cta + tph - 1) / tph + 1;
-  return 256 + round_up(n_heads * 4, 256) + grid * max_seg * gp * (int64_t)(value_dim + 2) * 4;
+  // per-head LUT area: fp32 entries with a fixed 256-row stride (upper bound), within the policy cap
+  const int64_t lut_bytes = (int64_t)((std::max(n_blocks, 1) + 7) / 8) * 8 * kLutC * gp * 4;
+  return mma_workspace_bytes(n_heads, grid, max_seg, gp, value_dim,
+                             (int64_t)n_heads * lut_bytes <= kGlobalLutMaxBytes ? lut_bytes : 0);
 }
 
 int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
@@ -542,6 +585,20 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
     p.err = reinterpret_cast<int*>(ws);
     p.counters = reinterpret_cast<int*>(ws + 256);
     p.slots = reinterpret_cast<float*>(ws + 256 + round_up(n_heads * 4, 256));
+    if (use_mma) {
+      // per-head LUTs built GPU-wide at kernel start when they fit the workspace policy
+      const int64_t lut_ws = kGlobalLutMaxBytes >= (int64_t)n_heads * p.lut_bytes ? p.lut_bytes : 0;
+      const MmaWsOffsets o = mma_workspace_offsets(n_heads, pl.grid, p.max_seg, pl.gp, dv, lut_ws);
+      p.slots = reinterpret_cast<float*>(ws + o.slots);
+      if (lut_ws && workspace_bytes >= o.total) {
+        p.lut_global = ws + o.luts;
+        p.lut_scale_global = reinterpret_cast<float*>(ws + o.scales);
+        if (int rc = launch_lut(p, pl.gp, pl.lut16, n_heads, st)) return rc;
+      }
+#ifdef SUNSHAPE_TRACE
+      p.trace = reinterpret_cast<unsigned long long*>(ws + (workspace_bytes - 4096 * 256) / 256 * 256);
+#endif
+    }
     DecodePlan pc = pl;
     pc.prm = p;
     if (int rc = use_mma ? launch_decode_mma(pc, dv, kv->value_dtype, st)

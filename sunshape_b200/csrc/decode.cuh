@@ -85,9 +85,14 @@ struct DecodeParams {
   float* partials;
   float* scores_out;
   // workspace
+  int lut_bytes;               // shared-memory LUT bytes of the tensor-core kernel
+  int merge_smem_bytes;        // bytes of the LUT/staging region usable by finish_segment
+  uint8_t* lut_global;         // per-head LUTs [n_heads][lut_bytes] built by lut_kernel, or null
+  float* lut_scale_global;     // [n_heads] inverse LUT scale (fp16 LUT) or 1
   float* slots;
   int* counters;
   int* err;
+  unsigned long long* trace;  // per-CTA marks (trace builds only)
   // partition
   int tph;            // tiles per head
   int64_t total_tiles;
@@ -196,23 +201,38 @@ __device__ __forceinline__ void load_value_row(const VT* src, float (&vf)[DPL]) 
   }
 }
 
+// q_s[g][d'] = q[row g of head hh][perm[d']] (scaled in the query dtype), zero for absent rows.
+// Loads are issued 8 per thread before any store so their latencies overlap.
+template <int GP, int NTHREADS>
+__device__ __forceinline__ void load_query_rows(const DecodeParams& p, int64_t hh, const int* perm_s, float* q_s,
+                                                int ctid) {
+  const int tot = GP * p.D;
+  for (int b0 = ctid; b0 < tot; b0 += NTHREADS * 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = b0 + u * NTHREADS;
+      const int g = e / p.D, dp = e - g * p.D;
+      float x = 0.f;
+      if (e < tot && g < p.Rc) {
+        x = load_as_float(p.q, (hh * p.R + p.r0 + g) * p.D + perm_s[dp], p.q_dtype);
+        if (p.has_scale) x = round_to_dtype(x * p.scale, p.q_dtype);
+      }
+      v[u] = x;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (b0 + u * NTHREADS < tot) q_s[b0 + u * NTHREADS] = v[u];
+  }
+}
+
 // Build the LUT (and the permuted, scaled query rows) for flat head hh.
 template <int GP, int NTHREADS>
 __device__ void build_lut_t(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
                             float* q_s, uint8_t* lut, int ctid) {
   constexpr int NH = GP / 4;
   named_barrier(kBarConsumers, NTHREADS);
-  for (int e = ctid; e < GP * p.D; e += NTHREADS) {
-    const int g = e / p.D, dp = e - g * p.D;
-    float v = 0.f;
-    if (g < p.Rc) {
-      const int64_t qrow = hh * p.R + p.r0 + g;
-      float x = load_as_float(p.q, qrow * p.D + perm_s[dp], p.q_dtype);
-      if (p.has_scale) x = round_to_dtype(x * p.scale, p.q_dtype);
-      v = x;
-    }
-    q_s[g * p.D + dp] = v;
-  }
+  load_query_rows<GP, NTHREADS>(p, hh, perm_s, q_s, ctid);
   named_barrier(kBarConsumers, NTHREADS);
   const int cbh = p.n_cb == 1 ? 0 : (int)((hh % p.kv_heads) % p.n_cb);
   const float* cb = p.cb + (int64_t)cbh * p.nb * p.C * p.bd;
@@ -299,6 +319,11 @@ __device__ void produce(const DecodeParams& p, int64_t tb, int64_t te, uint64_t*
 // Merge them; if this CTA is the head's only contributor write the result, else store
 // the CTA partial in the workspace slot and let the last contributor (atomic ticket)
 // merge all slots of the head.
+#ifdef SUNSHAPE_TRACE
+#define SUNSHAPE_FMARK(k) do { if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + (k)] = global_ns(); } while (0)
+#else
+#define SUNSHAPE_FMARK(k) ((void)0)
+#endif
 template <int GP, int DV, int NW>
 __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t hh, int64_t tb, int64_t grid,
                                int ctid, int* flag_s) {
@@ -336,8 +361,10 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
       if (d == 0) { slot[r * ROWF] = M; slot[r * ROWF + 1] = Lsum; }
     }
   }
+  SUNSHAPE_FMARK(8);
   if (!sole) {
     __threadfence();
+    SUNSHAPE_FMARK(9);
     named_barrier(kBarConsumers, NT);
     if (ctid == 0) {
       const int n_contrib = (int)(c_last - c_first + 1);
@@ -345,24 +372,62 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
       flag_s[0] = prev == n_contrib - 1;
     }
     named_barrier(kBarConsumers, NT);
+    SUNSHAPE_FMARK(10);
     if (flag_s[0]) {
       __threadfence();
+      // float offsets of the contributing CTAs' slots for this head, computed once
+      int64_t* offs = reinterpret_cast<int64_t*>(const_cast<float*>(stg) + NW * GP * ROWF + 2);
+      const int n_contrib = (int)(c_last - c_first + 1);
+      for (int k = ctid; k < n_contrib; k += NT) {
+        const int64_t c = c_first + k;
+        const int sl = (int)(hh - tile_start(c, p.total_tiles, grid) / p.tph);
+        offs[k] = (c * p.max_seg + sl) * GP * ROWF;
+      }
+      named_barrier(kBarConsumers, NT);
+      SUNSHAPE_FMARK(12);
+      // merge the contributing CTAs' slots: when they fit, gather them into shared memory first
+      // (one batch of independent loads; the slots were written long ago and may sit in HBM),
+      // then reduce from shared memory
+      const int slot_f = p.Rc * ROWF;
+      float* gath = reinterpret_cast<float*>(offs + n_contrib);
+      const bool staged = (int64_t)(reinterpret_cast<uint8_t*>(gath + (int64_t)n_contrib * slot_f) -
+                                    reinterpret_cast<const uint8_t*>(stg)) <= p.merge_smem_bytes;
+      const float* base = p.slots;
+      SUNSHAPE_FMARK(21);
+#ifdef SUNSHAPE_TRACE
+      if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + 23] = clock64();
+#endif
+      if (staged) {
+        const int tot = n_contrib * slot_f;
+        for (int b0 = ctid; b0 < tot; b0 += NT * 8) {   // 8 loads in flight per thread
+          float v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int idx = b0 + u * NT;
+            const int k = idx / slot_f;
+            v[u] = idx < tot ? __ldcg(p.slots + offs[min(k, n_contrib - 1)] + (idx - k * slot_f)) : 0.f;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (b0 + u * NT < tot) gath[b0 + u * NT] = v[u];
+        }
+        named_barrier(kBarConsumers, NT);
+      }
+      SUNSHAPE_FMARK(22);
+#pragma unroll 1
       for (int e = ctid; e < p.Rc * DV; e += NT) {
         const int r = e / DV, d = e - r * DV;
-        float M = NEG_INF, Lsum = 0.f, A = 0.f;
-        for (int64_t c = c_first; c <= c_last; ++c) {
-          const int sl = (int)(hh - tile_start(c, p.total_tiles, grid) / p.tph);
-          const float* src = p.slots + ((c * p.max_seg + sl) * GP + r) * ROWF;
-          const float m = __ldcg(src);
-          if (m == NEG_INF) continue;
-          const float l = __ldcg(src + 1), a = __ldcg(src + 2 + d);
-          if (m > M) {
-            const float sc = fast_exp2((M - m) * kLog2e);
-            Lsum = Lsum * sc + l;
-            A = A * sc + a;
-            M = m;
-          } else {
-            const float sc = fast_exp2((m - M) * kLog2e);
+        float M = NEG_INF;
+        for (int k = 0; k < n_contrib; ++k)
+          M = fmaxf(M, staged ? gath[k * slot_f + r * ROWF] : __ldcg(base + offs[k] + r * ROWF));
+        float Lsum = 0.f, A = 0.f;
+        if (M != NEG_INF) {
+          for (int k = 0; k < n_contrib; ++k) {
+            const float* src = staged ? gath + k * slot_f + r * ROWF : base + offs[k] + r * ROWF;
+            const float m = staged ? src[0] : __ldcg(src);
+            const float l = staged ? src[1] : __ldcg(src + 1);
+            const float a = staged ? src[2 + d] : __ldcg(src + 2 + d);
+            const float sc = fast_exp2((m - M) * kLog2e);   // m = -inf (empty slot) -> 0
             Lsum = fmaf(l, sc, Lsum);
             A = fmaf(a, sc, A);
           }
@@ -375,7 +440,13 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
           if (d == 0) { pr[0] = M; pr[1] = Lsum; }
         }
       }
+      named_barrier(kBarConsumers, NT);
+      SUNSHAPE_FMARK(13);
+#ifdef SUNSHAPE_TRACE
+      if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + 24] = clock64();
+#endif
       if (ctid == 0) atomicExch(&p.counters[hh], 0);
+      SUNSHAPE_FMARK(11);
     }
   }
 }

@@ -44,7 +44,11 @@ constexpr int kPrefetchAhead = 0;                // tiles prefetched into L2 bey
 #ifdef SUNSHAPE_TRACE
 #define SUNSHAPE_TRACE_ADD(slot, v) atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(p.err) + 64) + (slot), (unsigned long long)(v))
 #define SUNSHAPE_CLK() clock64()
+// per-CTA wall-clock marks (ns) in the trace area at the end of the workspace: [cta][0] start, [1] first tile landed,
+// [2] last tile consumed, [3] consumers done, [4 + 2k] segment k LUT ready, [5 + 2k] segment k merged
+#define SUNSHAPE_MARK(k) (p.trace[blockIdx.x * 32 + (k)] = global_ns())
 #else
+#define SUNSHAPE_MARK(k) ((void)0)
 #define SUNSHAPE_TRACE_ADD(slot, v) ((void)0)
 #define SUNSHAPE_CLK() 0ll
 #endif
@@ -106,7 +110,7 @@ __device__ __forceinline__ uint32_t p_chunk_offset(int row, int chunk) {
 }
 
 // LUT rows of one block for this thread: q block held in registers, codebook rows loaded
-// four at a time so their L2 latencies overlap; stores land in bank group b & 7.
+// eight at a time so their L2 latencies overlap; stores land in bank group b & 7.
 // Store one LUT entry (GP query rows of block b, codeword c): fp32 in GP/4 16-byte chunks,
 // or (L16) fp16 scaled by `scale` in GP/8 16-byte chunks -- for GP == 4 an 8-byte half of a
 // 16-byte slot shared by block groups kh = 2j and 2j + 1 (dst_base already points at the half).
@@ -138,18 +142,19 @@ __device__ __forceinline__ void store_lut_entry(uint8_t* dst_base, int c, const 
 
 template <int GP, int BD, bool L16>
 __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float* qblk, const float* cbb, bool active,
-                                             uint8_t* dst_base, int c0, float scale) {
+                                             uint8_t* dst_base, int c0, float scale, int c_hi) {
   float q[GP][BD];
 #pragma unroll
   for (int g = 0; g < GP; ++g)
 #pragma unroll
     for (int d = 0; d < BD; ++d) q[g][d] = active ? qblk[g * p.D + d] : 0.f;
-  for (int cb4 = c0; cb4 < p.C; cb4 += 128) {
-    float x[4][BD];
+  constexpr int U = 8;   // codeword rows in flight per thread
+  for (int cb4 = c0; cb4 < c_hi; cb4 += 32 * U) {
+    float x[U][BD];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < U; ++u) {
       const int c = cb4 + 32 * u;
-      const bool ok = active && c < p.C;
+      const bool ok = active && c < c_hi;
 #pragma unroll
       for (int d4 = 0; d4 < BD; d4 += 4) {   // codebook rows are 16-byte aligned (BD = 4 or 8)
         const float4 v = ok ? __ldg(reinterpret_cast<const float4*>(cbb + (int64_t)c * BD + d4))
@@ -157,10 +162,10 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
         x[u][d4] = v.x; x[u][d4 + 1] = v.y; x[u][d4 + 2] = v.z; x[u][d4 + 3] = v.w;
       }
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
+#pragma unroll 1   // cold code (runs once per LUT): keep it small for the instruction cache
+    for (int u = 0; u < U; ++u) {
       const int c = cb4 + 32 * u;
-      if (c >= p.C) break;
+      if (c >= c_hi) break;
       float v[GP];
 #pragma unroll
       for (int g = 0; g < GP; ++g) {
@@ -182,25 +187,21 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
 // of the entries times 1 / scale (exact).  The scale is left in *scale_s.
 template <int GP, bool L16>
 __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
-                            float* q_s, uint8_t* lut, int ctid, float* scale_s) {
+                            float* q_s, uint8_t* lut, int ctid, float* scale_s, int kh_lo = 0, int kh_hi = 1 << 20,
+                            int c_lo = 0, int c_hi = 1 << 20) {
+  c_hi = min(c_hi, p.C);
+  kh_hi = min(kh_hi, p.nbh);
   constexpr int NH = L16 ? (GP >= 8 ? GP / 8 : 1) : GP / 4;
   named_barrier(kBarConsumers, kConsumerThreadsM);
   if (L16 && ctid == 0) { scale_s[1] = 0.f; scale_s[2] = 0.f; }
-  for (int e = ctid; e < GP * p.D; e += kConsumerThreadsM) {
-    const int g = e / p.D, dp = e - g * p.D;
-    float v = 0.f;
-    if (g < p.Rc) {
-      const int64_t qrow = hh * p.R + p.r0 + g;
-      float x = load_as_float(p.q, qrow * p.D + perm_s[dp], p.q_dtype);
-      if (p.has_scale) x = round_to_dtype(x * p.scale, p.q_dtype);
-      v = x;
-    }
-    q_s[g * p.D + dp] = v;
-  }
+  load_query_rows<GP, kConsumerThreadsM>(p, hh, perm_s, q_s, ctid);
   named_barrier(kBarConsumers, kConsumerThreadsM);
   const int cbh = p.n_cb == 1 ? 0 : (int)((hh % p.kv_heads) % p.n_cb);
   const float* cb = p.cb + (int64_t)cbh * p.nb * p.C * p.bd;
   const int blo = ctid & 7, c0 = ctid >> 3;   // 8 bank groups x 32 codeword lanes
+#ifdef SUNSHAPE_TRACE
+  if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + 19] = global_ns();
+#endif
   float scale = 1.f;
   if constexpr (L16) {
     float qn = 0.f, cn = 0.f;
@@ -234,7 +235,10 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
     scale = bound > 0.f ? exp2f(fminf(100.f, floorf(log2f(32768.f / bound)))) : 1.f;
     if (ctid == 0) scale_s[0] = 1.f / scale;
   }
-  for (int kh = 0; kh < p.nbh; ++kh) {
+#ifdef SUNSHAPE_TRACE
+  if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + 20] = global_ns();
+#endif
+  for (int kh = kh_lo; kh < kh_hi; ++kh) {
     const int b = blo + 8 * kh;
     const bool active = b < p.nb && hslot_s[b] < 0;
     const float* qblk = q_s + (active ? b : 0) * p.bd;
@@ -242,11 +246,11 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
     uint8_t* dst = (L16 && GP == 4) ? lut + (int64_t)(kh >> 1) * kLutC * 128 + blo * 16 + (kh & 1) * 8
                                     : lut + (int64_t)kh * NH * kLutC * 128 + blo * 16;
     if (p.bd == 8) {
-      lut_rows_reg<GP, 8, L16>(p, qblk, cbb, active, dst, c0, scale);
+      lut_rows_reg<GP, 8, L16>(p, qblk, cbb, active, dst, c_lo + c0, scale, c_hi);
     } else if (p.bd == 4) {
-      lut_rows_reg<GP, 4, L16>(p, qblk, cbb, active, dst, c0, scale);
+      lut_rows_reg<GP, 4, L16>(p, qblk, cbb, active, dst, c_lo + c0, scale, c_hi);
     } else {
-      for (int c = c0; c < p.C; c += 32) {
+      for (int c = c_lo + c0; c < c_hi; c += 32) {
         float v[GP];
 #pragma unroll
         for (int g = 0; g < GP; ++g) v[g] = 0.f;
@@ -261,6 +265,99 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
     }
   }
   named_barrier(kBarConsumers, kConsumerThreadsM);
+}
+
+// Per-head LUTs for one decode launch, in exactly the shared-memory layout the decode kernel
+// uses, written to the workspace: one CTA per (KV head, block), one thread per codeword, so the
+// whole GPU builds all LUTs in a couple of memory round trips.  The decode kernel is launched as
+// a programmatic dependent of this grid: its producer warps start streaming values right away and
+// only its consumers wait (griddepcontrol.wait) before copying their first LUT.
+template <int GP, bool L16>
+__global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ DecodeParams p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  __shared__ float q_s[GP * 256];
+  __shared__ float red[2];
+  const int tid = threadIdx.x;
+  const int64_t hh = blockIdx.x;
+  const int b = blockIdx.y;                       // block (0 .. 8 * nbh - 1; padding blocks get zeros)
+  const int D = p.D, bd = p.bd;
+  // permuted, scaled query rows of this head (all blocks: the fp16 scale bounds every block)
+  for (int b0 = tid; b0 < GP * D; b0 += 256 * 4) {
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = b0 + u * 256;
+      const int g = e / D, dp = e - g * D;
+      float x = 0.f;
+      if (e < GP * D && g < p.Rc) {
+        x = load_as_float(p.q, (hh * p.R + p.r0 + g) * D + (int)__ldg(p.perm + dp), p.q_dtype);
+        if (p.has_scale) x = round_to_dtype(x * p.scale, p.q_dtype);
+      }
+      v[u] = x;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (b0 + u * 256 < GP * D) q_s[b0 + u * 256] = v[u];
+  }
+  if (tid == 0) { red[0] = 0.f; red[1] = 1.f; }
+  __syncthreads();
+  const int cbh = p.n_cb == 1 ? 0 : (int)((hh % p.kv_heads) % p.n_cb);
+  float scale = 1.f;
+  if constexpr (L16) {
+    float qn = 0.f;
+    for (int e = tid; e < GP * p.nb; e += 256) {
+      const int g = e / p.nb, bb = e - g * p.nb;
+      float a = 0.f;
+      for (int d = 0; d < bd; ++d) a = fmaf(q_s[g * D + bb * bd + d], q_s[g * D + bb * bd + d], a);
+      qn = fmaxf(qn, a);
+    }
+    qn = warp_max(qn);
+    if ((tid & 31) == 0) atomicMax(reinterpret_cast<int*>(&red[0]), __float_as_int(qn));
+    __syncthreads();
+    float cn;
+    if (p.cb_norm_max != nullptr) {
+      const float m = __ldg(p.cb_norm_max + cbh);
+      cn = m * m;
+    } else {   // fallback bound: scan this head's codebook (slow path, C ABI callers without norms)
+      cn = 0.f;
+      const float* cbf = p.cb + (int64_t)cbh * p.nb * p.C * bd;
+      for (int e = tid; e < p.nb * p.C * bd; e += 256) cn = fmaxf(cn, cbf[e] * cbf[e] * bd);
+      cn = warp_max(cn);
+      if ((tid & 31) == 0) atomicMax(reinterpret_cast<int*>(&red[1]), __float_as_int(cn));
+      __syncthreads();
+      cn = red[1];
+    }
+    const float bound = sqrtf(red[0]) * sqrtf(cn) * 1.001f;
+    scale = bound > 0.f ? exp2f(fminf(100.f, floorf(log2f(32768.f / bound)))) : 1.f;
+    if (b == 0 && tid == 0) p.lut_scale_global[hh] = 1.f / scale;
+  } else {
+    if (b == 0 && tid == 0) p.lut_scale_global[hh] = 1.f;
+  }
+  const int c = tid;
+  if (c >= p.C) return;
+  const bool active = b < p.nb && (p.heavy_mask == nullptr || p.heavy_mask[b] == 0);
+  float v[GP];
+#pragma unroll
+  for (int g = 0; g < GP; ++g) v[g] = 0.f;
+  if (active) {
+    const float* cr = p.cb + (((int64_t)cbh * p.nb + b) * p.C + c) * bd;
+    for (int d = 0; d < bd; ++d) {
+      const float x = __ldg(cr + d);
+#pragma unroll
+      for (int g = 0; g < GP; ++g) v[g] = fmaf(q_s[g * D + b * bd + d], x, v[g]);
+    }
+  }
+  const int kh = b >> 3, blo = b & 7;
+  constexpr int NH = L16 ? (GP >= 8 ? GP / 8 : 1) : GP / 4;
+  uint8_t* base = p.lut_global + hh * (int64_t)p.lut_bytes;
+  uint8_t* dst = (L16 && GP == 4) ? base + (int64_t)(kh >> 1) * kLutC * 128 + blo * 16 + (kh & 1) * 8
+                                  : base + (int64_t)kh * NH * kLutC * 128 + blo * 16;
+  store_lut_entry<GP, L16>(dst, c, v, scale);
+}
+
+template <int GP, bool L16>
+void launch_lut_t(const DecodeParams& prm, int n_heads, cudaStream_t st) {
+  lut_kernel<GP, L16><<<dim3(n_heads, prm.nbh * 8), 256, 0, st>>>(prm);
 }
 
 // Producer warp of the tensor-core kernel: TMA tensor boxes for values, bulk
@@ -380,6 +477,7 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   uint64_t* empty = full + kMaxStages;
   int* flag_s = reinterpret_cast<int*>(smem + 128);
   float* scale_s = reinterpret_cast<float*>(smem + 192);   // LUT scale (inverse), norm bounds
+  uint64_t* lut_bar = reinterpret_cast<uint64_t*>(smem + 232);   // LUT bulk copy completion
   int* perm_s = reinterpret_cast<int*>(smem + p.off_perm);
   int8_t* hslot_s = reinterpret_cast<int8_t*>(smem + p.off_hslot);
   int8_t* hlist_s = hslot_s + 32;                 // heavy block ids in slot order
@@ -394,10 +492,12 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   const int64_t te = tile_start(blockIdx.x + 1, p.total_tiles, grid);
 
   if (tid == 0) {
+    SUNSHAPE_MARK(0);
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kWarpsPerTileM);
     }
+    mbar_init(lut_bar, 1);
     fence_mbar_init();
     int n = 0;
     for (int b = 0; b < p.nb; ++b) {
@@ -410,9 +510,9 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   for (int i = tid; i < p.D; i += kThreadsM) perm_s[i] = (int)p.perm[i];
   __syncthreads();
   const int n_heavy = flag_s[2];
-  if (te <= tb) return;
 
   if (warp >= kWarpsM) {
+    if (te <= tb) return;
     produce_mma<DV>(p, tb, te, full, empty, stage0, n_heavy, lane, warp - kWarpsM);
     return;
   }
@@ -429,16 +529,43 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   const bool fast_idx = (p.nb & 7) == 0;
   const int gid = lane >> 2, tig = lane & 3;
 
+  if (te <= tb) return;
+  // LUTs come from the preceding lut_kernel grid (programmatic dependent launch)
+  if (p.lut_global != nullptr) asm volatile("griddepcontrol.wait;" ::: "memory");
   const long long tc0 = SUNSHAPE_CLK();
   long long t_wait = 0, t_lut = 0, t_end = 0;
+  uint32_t lut_phase_bit = 0;
   int64_t f = tb;
   while (f < te) {
     const int64_t hh = f / p.tph;
     const int64_t fend = min(te, (hh + 1) * p.tph);
     const int i0 = (int)(f - tb), i1 = (int)(fend - tb);
     const long long tl = SUNSHAPE_CLK();
-    build_lut_m<GP, L16>(p, hh, perm_s, hslot_s, q_s, lut, ctid, scale_s);
-    const float inv_scale = L16 ? scale_s[0] : 1.f;
+    float inv_scale = 1.f;
+    if (p.lut_global != nullptr) {
+      // the LUT region also served as staging for the last segment's partials: order those generic
+      // writes before the async-proxy copy, then bulk-copy this head's LUT from the workspace
+      fence_proxy_async_smem();
+      named_barrier(kBarConsumers, kConsumerThreadsM);
+      if (ctid == 0) {
+        mbar_arrive_expect_tx(lut_bar, (uint32_t)p.lut_bytes);
+        const uint8_t* src = p.lut_global + hh * (int64_t)p.lut_bytes;
+        for (int off = 0; off < p.lut_bytes; off += 32768)
+          bulk_g2s(lut + off, src + off, (uint32_t)min(32768, p.lut_bytes - off), lut_bar);
+      }
+      if (n_heavy > 0)   // permuted, scaled query rows for the dense heavy-block dot products
+        load_query_rows<GP, kConsumerThreadsM>(p, hh, perm_s, q_s, ctid);
+      mbar_wait(lut_bar, lut_phase_bit, p.err, kErrWaitFull);
+      lut_phase_bit ^= 1u;
+      if (L16) inv_scale = __ldcg(p.lut_scale_global + hh);
+      named_barrier(kBarConsumers, kConsumerThreadsM);
+    } else {
+      build_lut_m<GP, L16>(p, hh, perm_s, hslot_s, q_s, lut, ctid, scale_s);
+      if (L16) inv_scale = scale_s[0];
+    }
+#ifdef SUNSHAPE_TRACE
+    if (ctid == 0 && f - tb < 2 * p.tph && (hh - tb / p.tph) < 2) SUNSHAPE_MARK(4 + 2 * (int)(hh - tb / p.tph));
+#endif
     t_lut += SUNSHAPE_CLK() - tl;
 
     float m_run[GP], l_run[GP];
@@ -463,6 +590,10 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
       const long long tw = SUNSHAPE_CLK();
       mbar_wait(&full[s], phase, p.err, kErrWaitFull);
       t_wait += SUNSHAPE_CLK() - tw;
+#ifdef SUNSHAPE_TRACE
+      if (i == 0 && lane == 0) SUNSHAPE_MARK(1);
+      if (i == (int)(te - tb) - 1 && lane == 0) SUNSHAPE_MARK(2);
+#endif
       const int t0 = (int)(tb + i - seg_tile0) * kTileTokens;
       const int ntok = min(kTileTokens, p.T - t0);
       const int64_t row0 = hh * p.head_stride + t0;
@@ -705,8 +836,15 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
     named_barrier(kBarConsumers, kConsumerThreadsM);
     finish_segment<GP, DV, kWarpsM>(p, stg, hh, tb, grid, ctid, flag_s);
     t_end += SUNSHAPE_CLK() - te0;
+#ifdef SUNSHAPE_TRACE
+    if (ctid == 0 && (hh - tb / p.tph) < 2) SUNSHAPE_MARK(5 + 2 * (int)(hh - tb / p.tph));
+#endif
     f = fend;
   }
+#ifdef SUNSHAPE_TRACE
+  named_barrier(kBarConsumers, kConsumerThreadsM);
+  if (ctid == 0) SUNSHAPE_MARK(3);
+#endif
   if (lane == 0) {
     SUNSHAPE_TRACE_ADD(2, SUNSHAPE_CLK() - tc0);
     SUNSHAPE_TRACE_ADD(3, t_wait);
@@ -719,7 +857,23 @@ template <int GP, int DV, typename VT, bool L16>
 void launch_decode_mma_t(const DecodeLaunch& l, cudaStream_t st) {
   auto k = decode_mma_kernel<GP, DV, VT, L16>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem);
-  k<<<(unsigned)l.grid, kThreadsM, l.smem, st>>>(l.prm);
+  if (l.prm.lut_global == nullptr) {
+    k<<<(unsigned)l.grid, kThreadsM, l.smem, st>>>(l.prm);
+    return;
+  }
+  // programmatic dependent launch after lut_kernel: this grid may start while the LUTs are being
+  // built; its consumers wait for them with griddepcontrol.wait
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)l.grid);
+  cfg.blockDim = dim3(kThreadsM);
+  cfg.dynamicSmemBytes = (size_t)l.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k, l.prm);
 }
 
 

@@ -61,8 +61,10 @@ extern "C" int sunshape_decode_attention_noalloc(
     return sunshape::set_last_error(SUNSHAPE_E_INVALID, "batch / heads / query_len must be positive, q_heads a "
                                                         "multiple of kv_heads.");
   const int32_t n_heads = batch * kv_heads;
+  if (!codec) return sunshape::set_last_error(SUNSHAPE_E_INVALID, "codec descriptor is NULL.");
+  if (codec->block_dim <= 0) return sunshape::set_last_error(SUNSHAPE_E_INVALID, "block_dim must be positive.");
   const int64_t need = sunshape_decode_workspace_bytes(n_heads, kv->seq_len, (q_heads / kv_heads) * query_len,
-                                                       kv->value_dim);
+                                                       kv->value_dim, codec->head_dim / codec->block_dim);
   if (need > (int64_t)SUNSHAPE_NOALLOC_SCRATCH_BYTES)
     return sunshape::set_last_error(
         SUNSHAPE_E_WORKSPACE,
