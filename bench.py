@@ -270,7 +270,7 @@ def run_ours(args, cfg: DecodeConfig):
                                      passthrough_blocks=codec.mixed_high_precision_blocks if cfg.n_heavy else None,
                                      head_dim=cfg.head_dim, block_dim=cfg.block_dim)
     stream = torch.cuda.current_stream(dev)
-    sharded = KVShardedDecode(codec) if world > 1 else None
+    sharded = KVShardedDecode(codec, exchange=args.exchange) if world > 1 else None
     out = torch.empty(cfg.batch, cfg.q_heads, 1, cfg.head_dim, device=dev, dtype=value.dtype)
 
     if world == 1:
@@ -281,7 +281,7 @@ def run_ours(args, cfg: DecodeConfig):
     else:
         def step():
             sharded(query, keys, value, scale=scale)
-        launches_per_step = 3   # lut_kernel + decode_mma_kernel + merge (NCCL all-gather not counted)
+        launches_per_step = 3   # lut_kernel + decode_mma_kernel + merge (or xmerge); an NCCL all-gather is not counted
 
     # decode kernel alone (events around the launch on its stream) for the roofline
     def kernel_only():
@@ -373,7 +373,7 @@ def run_ours(args, cfg: DecodeConfig):
         "config": {"workload": f"{cfg.name}: batch {cfg.batch}, {cfg.q_heads}/{cfg.kv_heads} heads, head_dim "
                                f"{cfg.head_dim}, context {cfg.seq_len}, block_dim {cfg.block_dim}, "
                                f"{cfg.n_centroids} codewords, {cfg.n_heavy} heavy blocks",
-                   "global_batch": cfg.batch, "seq_len": cfg.seq_len, "parallelism": f"kv-seq-split{world}",
+                   "global_batch": cfg.batch, "seq_len": cfg.seq_len, "parallelism": f"kv-seq-split{world}", "exchange": args.exchange if world > 1 else None,
                    "kv_tokens_per_step": total_tokens, "bytes_per_kv_token": cfg.bytes_per_kv_token(),
                    "l2": "inputs larger than L2 (no flush needed)"},
         "hbm_gbs": achieved, "query_scores_per_s": value_tps * cfg.group,
@@ -460,6 +460,8 @@ def main():
     ap.add_argument("--workload", default="c5", choices=sorted(CONFIGS))
     ap.add_argument("--no-extra", action="store_true", help="skip the N=1 figures for the other configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
+                    help="N>1 merge: NCCL all-gather + merge kernel, or peer-memory stores from the decode kernel")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.workload]

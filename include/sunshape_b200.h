@@ -130,6 +130,39 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
                               float scale, void* out, int32_t out_dtype, float* partials,
                               void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ---- KV-sequence split across GPUs, exchange over peer memory (no reference counterpart: the
+ * reference has no distributed code).  Each rank holds one exchange buffer, allocated with
+ * sunshape_peer_alloc and mapped into every other rank's process with sunshape_peer_open (CUDA
+ * IPC); sunshape_peer_buffer_bytes gives its size. */
+typedef struct sunshape_peer_group {
+  int32_t rank;
+  int32_t world;          /* 2 .. 8 */
+  void* buffers[8];       /* buffers[r] = rank r's exchange buffer as mapped in this process */
+} sunshape_peer_group_t;
+
+int64_t sunshape_peer_buffer_bytes(int32_t world, int64_t rows, int32_t value_dim, int32_t n_heads);
+/* cudaMalloc + zero-fill a buffer on the current device; *ipc_handle receives 64 bytes (host). */
+int sunshape_peer_alloc(int64_t bytes, void** dev_ptr, void* ipc_handle);
+/* Map another process's buffer (from its 64-byte handle) into this process. */
+int sunshape_peer_open(const void* ipc_handle, void** dev_ptr);
+int sunshape_peer_close(void* dev_ptr);
+int sunshape_peer_free(void* dev_ptr);
+
+/* sunshape_decode_attention over this rank's KV shard (tokens [start_r, end_r) of every head),
+ * producing the full output on every rank: the decode kernel stores each head's rank-local
+ * (m, l, acc) rows into every rank's exchange buffer over NVLink and bumps that rank's per-head
+ * arrival counter; a merge kernel waits (bounded) for all ranks' rows of each head and writes
+ * out [batch, q_heads, query_len, value_dim].  All ranks must make the same sequence of calls.
+ * Requires G * query_len <= 16 rows per KV head and 16-bit values. */
+int sunshape_decode_attention_peers(const sunshape_codec_t* codec, const sunshape_kv_t* kv,
+                                    const void* query, int32_t query_dtype,
+                                    int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t query_len,
+                                    const void* mask, int32_t mask_dtype,
+                                    int64_t mask_sb, int64_t mask_sh, int64_t mask_sq,
+                                    float scale, void* out, int32_t out_dtype,
+                                    const sunshape_peer_group_t* group,
+                                    void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Size of the scratch array built into the library for sunshape_decode_attention_noalloc. */
 #define SUNSHAPE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 

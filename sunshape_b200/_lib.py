@@ -27,7 +27,9 @@ _DTYPE_CODE = {
 EXPORTED_SYMBOLS = (
     "sunshape_abi_version", "sunshape_last_error", "sunshape_encode", "sunshape_dequantize",
     "sunshape_attention_scores", "sunshape_decode_workspace_bytes", "sunshape_decode_attention",
-    "sunshape_merge_partials", "sunshape_decode_attention_noalloc",
+    "sunshape_merge_partials", "sunshape_decode_attention_noalloc", "sunshape_peer_buffer_bytes",
+    "sunshape_peer_alloc", "sunshape_peer_open", "sunshape_peer_close", "sunshape_peer_free",
+    "sunshape_decode_attention_peers",
 )
 
 
@@ -57,6 +59,10 @@ class KVDesc(ctypes.Structure):
         ("seq_len", ctypes.c_int32),
         ("head_stride", ctypes.c_int64),
     ]
+
+
+class PeerGroupDesc(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("buffers", ctypes.c_void_p * 8)]
 
 
 _lib = None
@@ -89,6 +95,17 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sunshape_decode_attention_noalloc.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64,
                                                           i64, f32, vp, i32, vp, vp]
         lib.sunshape_decode_attention_noalloc.restype = ctypes.c_int
+        lib.sunshape_peer_buffer_bytes.argtypes = [i32, i64, i32, i32]
+        lib.sunshape_peer_buffer_bytes.restype = ctypes.c_int64
+        lib.sunshape_peer_alloc.argtypes = [i64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+        lib.sunshape_peer_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.sunshape_peer_close.argtypes = [vp]
+        lib.sunshape_peer_free.argtypes = [vp]
+        for name in ("sunshape_peer_alloc", "sunshape_peer_open", "sunshape_peer_close", "sunshape_peer_free",
+                     "sunshape_decode_attention_peers"):
+            getattr(lib, name).restype = ctypes.c_int
+        lib.sunshape_decode_attention_peers.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64, i64,
+                                                        f32, vp, i32, ctypes.POINTER(PeerGroupDesc), vp, i64, vp]
         for name in ("sunshape_encode", "sunshape_dequantize", "sunshape_attention_scores",
                      "sunshape_decode_attention", "sunshape_merge_partials"):
             getattr(lib, name).restype = ctypes.c_int
@@ -233,3 +250,18 @@ def merge_partials(parts: torch.Tensor, out: torch.Tensor) -> None:
         _check(load_library().sunshape_merge_partials(
             ptr(parts), int(parts.shape[0]), int(parts.shape[1]), int(parts.shape[2] - 2), ptr(out),
             dtype_code(out), stream_ptr(dev)))
+
+
+def decode_attention_peers(cd: CodecDesc, kd: KVDesc, query: torch.Tensor, batch: int, q_heads: int, kv_heads: int,
+                           query_len: int, mask: torch.Tensor | None, mask_strides: tuple[int, int, int],
+                           scale: float | None, out: torch.Tensor, group: PeerGroupDesc) -> None:
+    dev = require_cuda(query, out, mask)
+    lib = load_library()
+    with torch.cuda.device(dev):
+        ws = decode_workspace(dev, batch * kv_heads, kd.seq_len, (q_heads // kv_heads) * query_len, kd.value_dim,
+                              cd.head_dim // cd.block_dim)
+        _check(lib.sunshape_decode_attention_peers(
+            ctypes.byref(cd), ctypes.byref(kd), ptr(query), dtype_code(query), batch, q_heads, kv_heads, query_len,
+            ptr(mask), dtype_code(mask) if mask is not None else F32, *mask_strides,
+            math.nan if scale is None else float(scale), ptr(out), dtype_code(out), ctypes.byref(group), ptr(ws),
+            ws.numel(), stream_ptr(dev)))

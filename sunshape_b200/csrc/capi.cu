@@ -35,6 +35,70 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, int n_par
   }
 }
 
+// Peer exchange buffer layout (bytes): [recv: 2 x world x rows x (DV + 2) fp32 | arrive: 2 x n_heads
+// u32 | step u32, done u32], each part 256-byte aligned.
+struct PeerLayout { int64_t recv, arrive, step, total; };
+inline PeerLayout peer_layout(int world, int64_t rows, int dv, int n_heads) {
+  PeerLayout l;
+  l.recv = 0;
+  l.arrive = ((int64_t)2 * world * rows * (dv + 2) * 4 + 255) / 256 * 256;
+  l.step = l.arrive + ((int64_t)2 * n_heads * 4 + 255) / 256 * 256;
+  l.total = l.step + 256;
+  return l;
+}
+
+// Cross-GPU merge: one CTA per KV head waits (bounded) until every rank's rows of the head have
+// arrived in this rank's exchange buffer, merges them in rank order and writes the output; the
+// last CTA advances the step counter (its parity selects the buffer half of the next call).
+__global__ void xmerge_kernel(float* recv, unsigned int* arrive, unsigned int* step, unsigned int* done, int world,
+                              int64_t rows, int R, int dv, int n_heads, void* out, int out_dtype, int* err) {
+  __shared__ unsigned parity_s;
+  const int64_t hh = blockIdx.x;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  if (threadIdx.x == 0) {
+    const unsigned parity = *reinterpret_cast<volatile unsigned int*>(step) & 1u;
+    parity_s = parity;
+    unsigned int* a = arrive + (int64_t)parity * n_heads + hh;
+    const uint64_t t0 = global_ns();
+    while (true) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+      if ((int)v >= world) break;
+      if (global_ns() - t0 > kWaitLimitNs) { record_error(err, 104); break; }
+      __nanosleep(64);
+    }
+  }
+  __syncthreads();
+  const unsigned parity = parity_s;
+  for (int e = threadIdx.x; e < R * dv; e += blockDim.x) {
+    const int r = e / dv, d = e - r * dv;
+    const int64_t orow = hh * R + r;
+    float M = NEG_INF;
+    for (int k = 0; k < world; ++k)
+      M = fmaxf(M, __ldcv(recv + ((int64_t)(parity * world + k) * rows + orow) * (dv + 2)));
+    float Lsum = 0.f, A = 0.f;
+    if (M != NEG_INF) {
+      for (int k = 0; k < world; ++k) {
+        const float* src = recv + ((int64_t)(parity * world + k) * rows + orow) * (dv + 2);
+        const float sc = fast_exp2((__ldcv(src) - M) * kLog2e);
+        Lsum = fmaf(__ldcv(src + 1), sc, Lsum);
+        A = fmaf(__ldcv(src + 2 + d), sc, A);
+      }
+    }
+    store_from_float(out, orow * dv + d, out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    arrive[(int64_t)parity * n_heads + hh] = 0u;   // reused two calls later
+    __threadfence();
+    if (atomicAdd(done, 1u) == (unsigned)gridDim.x - 1) {
+      *done = 0u;
+      __threadfence();
+      atomicAdd(step, 1u);
+    }
+  }
+}
+
 }  // namespace sunshape
 
 using namespace sunshape;
@@ -532,11 +596,52 @@ int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_
                              (int64_t)n_heads * lut_bytes <= kGlobalLutMaxBytes ? lut_bytes : 0);
 }
 
+static int decode_impl(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
+                       int32_t query_dtype, int32_t batch, int32_t q_heads, int32_t kv_heads,
+                       int32_t query_len, const void* mask, int32_t mask_dtype, int64_t mask_sb,
+                       int64_t mask_sh, int64_t mask_sq, float scale, void* out, int32_t out_dtype,
+                       float* partials, void* workspace, int64_t workspace_bytes, void* stream,
+                       const sunshape_peer_group_t* group);
+
 int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
                               int32_t query_dtype, int32_t batch, int32_t q_heads, int32_t kv_heads,
                               int32_t query_len, const void* mask, int32_t mask_dtype, int64_t mask_sb,
                               int64_t mask_sh, int64_t mask_sq, float scale, void* out, int32_t out_dtype,
                               float* partials, void* workspace, int64_t workspace_bytes, void* stream) {
+  return decode_impl(codec, kv, query, query_dtype, batch, q_heads, kv_heads, query_len, mask, mask_dtype, mask_sb,
+                     mask_sh, mask_sq, scale, out, out_dtype, partials, workspace, workspace_bytes, stream, nullptr);
+}
+
+int sunshape_decode_attention_peers(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
+                                    int32_t query_dtype, int32_t batch, int32_t q_heads, int32_t kv_heads,
+                                    int32_t query_len, const void* mask, int32_t mask_dtype, int64_t mask_sb,
+                                    int64_t mask_sh, int64_t mask_sq, float scale, void* out, int32_t out_dtype,
+                                    const sunshape_peer_group_t* group, void* workspace, int64_t workspace_bytes,
+                                    void* stream) {
+  if (!group) return fail(SUNSHAPE_E_INVALID, "peer group is NULL.");
+  if (group->world < 2 || group->world > 8 || group->rank < 0 || group->rank >= group->world)
+    return fail(SUNSHAPE_E_INVALID, "peer group: world must be 2..8 and 0 <= rank < world.");
+  for (int r = 0; r < group->world; ++r)
+    if (!group->buffers[r]) return fail(SUNSHAPE_E_INVALID, "peer group: missing exchange buffer.");
+  if (!out) return fail(SUNSHAPE_E_INVALID, "out pointer is NULL.");
+  if (!kv || kv->value_dtype == SUNSHAPE_F32)
+    return fail(SUNSHAPE_E_UNSUPPORTED, "the peer exchange path needs 16-bit values.");
+  if (q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads || (q_heads / kv_heads) * query_len > 16)
+    return fail(SUNSHAPE_E_UNSUPPORTED, "the peer exchange path needs G * query_len <= 16.");
+  return decode_impl(codec, kv, query, query_dtype, batch, q_heads, kv_heads, query_len, mask, mask_dtype, mask_sb,
+                     mask_sh, mask_sq, scale, out, out_dtype, nullptr, workspace, workspace_bytes, stream, group);
+}
+
+int64_t sunshape_peer_buffer_bytes(int32_t world, int64_t rows, int32_t value_dim, int32_t n_heads) {
+  return peer_layout(world, rows, value_dim, n_heads).total;
+}
+
+static int decode_impl(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,
+                       int32_t query_dtype, int32_t batch, int32_t q_heads, int32_t kv_heads,
+                       int32_t query_len, const void* mask, int32_t mask_dtype, int64_t mask_sb,
+                       int64_t mask_sh, int64_t mask_sq, float scale, void* out, int32_t out_dtype,
+                       float* partials, void* workspace, int64_t workspace_bytes, void* stream,
+                       const sunshape_peer_group_t* group) {
   if (int rc = check_codec(codec)) return rc;
   if (int rc = check_kv(kv, codec, true)) return rc;
   if (int rc = check_decode_codec(codec, kv)) return rc;
@@ -565,6 +670,8 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
                           : plan_decode(pl, nb, codec->n_centroids, codec->head_dim, dv, dtype_size(kv->value_dtype),
                                         n_heavy, codec->block_dim, hsz, false, n_heads, kv->seq_len, R, why);
   if (!ok) return fail(SUNSHAPE_E_UNSUPPORTED, why);
+  if (group && pl.chunk_rows < R)
+    return fail(SUNSHAPE_E_UNSUPPORTED, "the peer exchange path needs all query rows of a KV head in one launch.");
   if (use_mma) {
     const int64_t rows_total = (int64_t)(n_heads - 1) * kv->head_stride + kv->seq_len;
     if (int rc = make_value_map(&pl.prm.tmap_v, kv->value, kv->value_dtype, dv, rows_total)) return rc;
@@ -582,6 +689,19 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
     p.mask = mask; p.mask_dtype = mask_dtype; p.msb = mask_sb; p.msh = mask_sh; p.msq = mask_sq;
     p.scale = scale; p.has_scale = std::isnan(scale) ? 0 : 1;
     p.out = out; p.out_dtype = out_dtype; p.partials = partials;
+    if (group) {   // rank-local results go to the exchange buffers; xmerge_kernel writes out
+      const PeerLayout lay = peer_layout(group->world, (int64_t)n_heads * R, dv, n_heads);
+      p.out = nullptr;
+      p.xworld = group->world;
+      p.xrank = group->rank;
+      p.x_rows = (int64_t)n_heads * R;
+      for (int r = 0; r < group->world; ++r) {
+        p.xrecv[r] = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(group->buffers[r]) + lay.recv);
+        p.xarrive[r] = reinterpret_cast<unsigned int*>(reinterpret_cast<uint8_t*>(group->buffers[r]) + lay.arrive);
+      }
+      p.xstep = reinterpret_cast<const unsigned int*>(reinterpret_cast<uint8_t*>(group->buffers[group->rank]) +
+                                                      lay.step);
+    }
     p.err = reinterpret_cast<int*>(ws);
     p.counters = reinterpret_cast<int*>(ws + 256);
     p.slots = reinterpret_cast<float*>(ws + 256 + round_up(n_heads * 4, 256));
@@ -604,6 +724,15 @@ int sunshape_decode_attention(const sunshape_codec_t* codec, const sunshape_kv_t
     if (int rc = use_mma ? launch_decode_mma(pc, dv, kv->value_dtype, st)
                          : launch_decode<false>(pc, dv, kv->value_dtype, st))
       return rc;
+    if (group) {
+      const PeerLayout lay = peer_layout(group->world, (int64_t)n_heads * R, dv, n_heads);
+      uint8_t* own = reinterpret_cast<uint8_t*>(group->buffers[group->rank]);
+      unsigned int* stp = reinterpret_cast<unsigned int*>(own + lay.step);
+      xmerge_kernel<<<n_heads, 128, 0, st>>>(reinterpret_cast<float*>(own + lay.recv),
+                                              reinterpret_cast<unsigned int*>(own + lay.arrive), stp, stp + 1,
+                                              group->world, (int64_t)n_heads * R, R, dv, n_heads, out, out_dtype,
+                                              p.err);
+    }
   }
   return cuda_status("decode launch");
 }

@@ -92,6 +92,14 @@ struct DecodeParams {
   float* slots;
   int* counters;
   int* err;
+  // cross-GPU exchange over peer memory (xworld > 0): the final per-head partial rows go to every
+  // rank's receive buffer [2 parities][xworld][x_rows][DV + 2], then the rank's arrival counter
+  // [2][n_heads] is bumped; the step counter's parity selects the buffer
+  int xworld, xrank;
+  int64_t x_rows;
+  float* xrecv[8];
+  unsigned int* xarrive[8];
+  const unsigned int* xstep;
   unsigned long long* trace;  // per-CTA marks (trace builds only)
   // partition
   int tph;            // tiles per head
@@ -319,6 +327,35 @@ __device__ void produce(const DecodeParams& p, int64_t tb, int64_t te, uint64_t*
 // Merge them; if this CTA is the head's only contributor write the result, else store
 // the CTA partial in the workspace slot and let the last contributor (atomic ticket)
 // merge all slots of the head.
+// Final (m, l, acc) of output row `orow` (column d): to the output / partial buffers, and in
+// cross-GPU mode to every rank's receive buffer (NVLink peer stores).
+template <int DV>
+__device__ __forceinline__ void emit_row(const DecodeParams& p, int64_t orow, int d, float M, float Lsum, float A,
+                                         unsigned parity) {
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
+  if (p.partials) {
+    float* pr = p.partials + orow * (int64_t)(DV + 2);
+    pr[2 + d] = A;
+    if (d == 0) { pr[0] = M; pr[1] = Lsum; }
+  }
+  for (int r = 0; r < p.xworld; ++r) {
+    float* dst = p.xrecv[r] + ((int64_t)(parity * p.xworld + p.xrank) * p.x_rows + orow) * (DV + 2);
+    dst[2 + d] = A;
+    if (d == 0) { dst[0] = M; dst[1] = Lsum; }
+  }
+}
+
+// After every thread emitted its rows of head hh: make the peer stores visible system-wide, then
+// count this rank's arrival for hh on every rank.
+__device__ __forceinline__ void signal_peers(const DecodeParams& p, int64_t hh, unsigned parity, int ctid, int nt) {
+  if (p.xworld == 0) return;
+  __threadfence_system();
+  named_barrier(kBarConsumers, nt);
+  if (ctid == 0)
+    for (int r = 0; r < p.xworld; ++r) atomicAdd_system(p.xarrive[r] + (int64_t)parity * p.n_heads + hh, 1u);
+}
+
 #ifdef SUNSHAPE_TRACE
 #define SUNSHAPE_FMARK(k) do { if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + (k)] = global_ns(); } while (0)
 #else
@@ -335,6 +372,7 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
   const bool sole = c_first == c_last;
   const int seg_local = (int)(hh - tb / p.tph);
   float* slot = p.slots + ((int64_t)blockIdx.x * p.max_seg + seg_local) * GP * ROWF;
+  const unsigned parity = p.xworld ? (*reinterpret_cast<const volatile unsigned int*>(p.xstep) & 1u) : 0u;
   for (int e = ctid; e < p.Rc * DV; e += NT) {
     const int r = e / DV, d = e - r * DV;
     float M = NEG_INF;
@@ -349,19 +387,14 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
       }
     }
     if (sole) {
-      const int64_t orow = hh * p.R + p.r0 + r;
-      if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
-      if (p.partials) {
-        float* pr = p.partials + orow * (int64_t)(DV + 2);
-        pr[2 + d] = A;
-        if (d == 0) { pr[0] = M; pr[1] = Lsum; }
-      }
+      emit_row<DV>(p, hh * p.R + p.r0 + r, d, M, Lsum, A, parity);
     } else {
       slot[r * ROWF + 2 + d] = A;
       if (d == 0) { slot[r * ROWF] = M; slot[r * ROWF + 1] = Lsum; }
     }
   }
   SUNSHAPE_FMARK(8);
+  if (sole) signal_peers(p, hh, parity, ctid, NT);
   if (!sole) {
     __threadfence();
     SUNSHAPE_FMARK(9);
@@ -432,14 +465,9 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
             A = fmaf(a, sc, A);
           }
         }
-        const int64_t orow = hh * p.R + p.r0 + r;
-        if (p.out) store_from_float(p.out, orow * DV + d, p.out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
-        if (p.partials) {
-          float* pr = p.partials + orow * (int64_t)(DV + 2);
-          pr[2 + d] = A;
-          if (d == 0) { pr[0] = M; pr[1] = Lsum; }
-        }
+        emit_row<DV>(p, hh * p.R + p.r0 + r, d, M, Lsum, A, parity);
       }
+      signal_peers(p, hh, parity, ctid, NT);
       named_barrier(kBarConsumers, NT);
       SUNSHAPE_FMARK(13);
 #ifdef SUNSHAPE_TRACE

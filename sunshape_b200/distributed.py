@@ -14,11 +14,13 @@ the identical final output:
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from .vllm_attn_backend import SunShapeQuantizedKeys, decode_partials
+from .vllm_attn_backend import SunShapeQuantizedKeys, _apply_quantized_attention, decode_partials
 
 
 def kv_shard_bounds(seq_len: int, world_size: int, rank: int) -> tuple[int, int]:
@@ -51,13 +53,64 @@ def merge_gathered(gathered: torch.Tensor, out_shape, out_dtype) -> torch.Tensor
     return out.view(*out_shape)
 
 
-class KVShardedDecode:
-    """Decode attention over a KV cache whose sequence is split across the ranks of ``group``."""
+class PeerGroup:
+    """One exchange buffer per rank, mapped into every rank's process (CUDA IPC), for the fused
+    cross-GPU merge: the decode kernel stores its rank-local results straight into the peers'
+    buffers over NVLink (see ``sunshape_decode_attention_peers``)."""
 
-    def __init__(self, codec, group=None):
+    def __init__(self, nbytes: int, device: torch.device, group=None):
+        lib = _lib.load_library()
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise RuntimeError("the peer exchange supports at most 8 ranks")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        with torch.cuda.device(device):
+            _lib._check(lib.sunshape_peer_alloc(int(nbytes), ctypes.byref(own), handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._own, self._opened = own.value, []
+        bufs = []
+        with torch.cuda.device(device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bufs.append(own.value)
+                    continue
+                hb = (ctypes.c_char * 64).from_buffer_copy(h)
+                pp = ctypes.c_void_p()
+                _lib._check(lib.sunshape_peer_open(hb, ctypes.byref(pp)))
+                bufs.append(pp.value)
+                self._opened.append(pp.value)
+        self.desc = _lib.PeerGroupDesc(self.rank, self.world, (ctypes.c_void_p * 8)(*(bufs + [None] * (8 - len(bufs)))))
+        self.device = device
+
+    def close(self):
+        lib = _lib.load_library()
+        with torch.cuda.device(self.device):
+            for pp in self._opened:
+                lib.sunshape_peer_close(ctypes.c_void_p(pp))
+            if self._own:
+                lib.sunshape_peer_free(ctypes.c_void_p(self._own))
+        self._opened, self._own = [], None
+
+
+class KVShardedDecode:
+    """Decode attention over a KV cache whose sequence is split across the ranks of ``group``.
+
+    ``exchange="nccl"`` (default): partials, one NCCL all-gather, merge kernel.
+    ``exchange="peer"`` (CUDA, 16-bit values, at most 8 ranks): ranks write their per-head results
+    straight into every peer's exchange buffer from inside the decode kernel (CUDA IPC mappings,
+    NVLink stores, system-scope arrival counters), then one merge kernel per rank combines them; no
+    library collective.  On 8 B200s at the c5 shape it measured 131 us per step against 120 us for
+    the NCCL path, so it is opt-in.
+    """
+
+    def __init__(self, codec, group=None, exchange: str = "nccl"):
         self.codec = codec
         self.group = group
+        self.exchange = exchange
         self._partials = None
+        self._peers: dict = {}
 
     def partials(self, query, key: SunShapeQuantizedKeys, value, attn_mask=None, scale=None) -> torch.Tensor:
         B, Hq, L, _ = query.shape
@@ -68,8 +121,27 @@ class KVShardedDecode:
         return decode_partials(codec=self.codec, query=query, key=key, value=value, attn_mask=attn_mask,
                                scale=scale, partials=self._partials)
 
+    def _peer_group(self, query, value) -> "PeerGroup | None":
+        if self.exchange != "peer" or not query.is_cuda or value.dtype == torch.float32:
+            return None
+        B, Hq, L, _ = query.shape
+        Hkv, Dv = value.shape[1], value.shape[-1]
+        if (Hq // Hkv) * L > 16 or dist.get_world_size(self.group) > 8:
+            return None
+        key = (B * Hq * L, Dv, B * Hkv, query.device)
+        pg = self._peers.get(key)
+        if pg is None:
+            nbytes = _lib.load_library().sunshape_peer_buffer_bytes(dist.get_world_size(self.group), B * Hq * L, Dv,
+                                                                    B * Hkv)
+            pg = self._peers[key] = PeerGroup(nbytes, query.device, self.group)
+        return pg
+
     def forward(self, query, key: SunShapeQuantizedKeys, value, attn_mask=None, scale=None) -> torch.Tensor:
         """Rank-local shard in, full merged output [B, Hq, L, Dv] (value dtype) out, on every rank."""
+        pg = self._peer_group(query, value)
+        if pg is not None:
+            return _apply_quantized_attention(codec=self.codec, query=query, key=key, value=value,
+                                              attn_mask=attn_mask, scale=scale, peer_group=pg.desc)
         part = self.partials(query, key, value, attn_mask, scale)
         gathered = gather_partials(part, self.group)
         B, Hq, L, _ = query.shape

@@ -312,7 +312,7 @@ def _kv_layout(value, idx, heavy, B, H, T):
 def _apply_quantized_attention(*, codec, query: torch.Tensor, key: SunShapeQuantizedKeys, value: torch.Tensor,
                                attn_mask: torch.Tensor | None, scale: float | None,
                                partials: torch.Tensor | None = None, out: torch.Tensor | None = None,
-                               write_output: bool = True):
+                               write_output: bool = True, peer_group=None):
     """vllm_attn_backend.py:216-253 as one fused launch.
 
     query [B, Hq, L, D], value [B, Hkv, T, Dv] -> output [B, Hq, L, Dv] in value.dtype.
@@ -339,7 +339,10 @@ def _apply_quantized_attention(*, codec, query: torch.Tensor, key: SunShapeQuant
     if B == 0:
         return out
     kd = _lib.kv_desc(idx, heavy, v, T, hs, Dv)
-    _lib.decode_attention(desc, kd, q, B, Hq, Hkv, L, mask, mstr, scale, out, partials)
+    if peer_group is not None:
+        _lib.decode_attention_peers(desc, kd, q, B, Hq, Hkv, L, mask, mstr, scale, out, peer_group)
+    else:
+        _lib.decode_attention(desc, kd, q, B, Hq, Hkv, L, mask, mstr, scale, out, partials)
     return out
 
 
