@@ -362,9 +362,10 @@ def run_ours(args, cfg: DecodeConfig):
     achieved = alg / (kernel_ms * 1e-3) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", f"decode_kernel_{cfg.name}.json")
-    if os.path.exists(tp) and world == 1:
+    if os.path.exists(tp):
+        # DRAM bytes per algorithmic byte from one ncu capture, applied to this launch's bytes
         with open(tp) as f:
-            traffic = json.load(f).get("traffic_bytes_per_launch")
+            traffic = round(alg * json.load(f)["traffic_over_algorithmic"])
     res = {
         "metric": METRIC, "value": value_tps, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
@@ -460,11 +461,15 @@ def main():
     ap.add_argument("--workload", default="c5", choices=sorted(CONFIGS))
     ap.add_argument("--no-extra", action="store_true", help="skip the N=1 figures for the other configs")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--seq-len", type=int, default=0,
+                    help="override the workload's context length (small cases for profiler captures)")
     ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
                     help="N>1 merge: NCCL all-gather + merge kernel, or peer-memory stores from the decode kernel")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.workload]
+    if args.seq_len:
+        cfg = cfg.with_(seq_len=args.seq_len)
 
     if args.impl == "reference":
         res = run_reference(args, cfg)
