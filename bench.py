@@ -421,8 +421,20 @@ def run_extra_configs(args):
             nkeys = kk.shape[0] * kk.shape[1] * kk.shape[2]
             byt = nkeys * (cfg.head_dim * 4 + cfg.n_blocks)
             extra["c3_encode"] = {"keys_per_s": nkeys / (ms_e * 1e-3), "ms": ms_e, "hbm_gbs": byt / (ms_e * 1e-3) / 1e9,
-                                  "argmin_compares_per_s": nkeys * cfg.n_blocks * cfg.n_centroids / (ms_e * 1e-3)}
+                                  "argmin_compares_per_s": nkeys * cfg.n_blocks * cfg.n_centroids / (ms_e * 1e-3),
+                                  "kernel": "encode_kernel (fp32 keys, CUDA cores)"}
+            # bf16 keys (what a model hands the encoder): the tcgen05 kernel, 3 tf32 MMAs per block
+            kb = kk.to(torch.bfloat16)
             del kk
+            ms_b = time_steps(lambda: codec.quantize_packed(kb, kv_heads=cfg.kv_heads), 5, 2,
+                              torch.cuda.current_stream(dev)) / 5
+            flops = 2.0 * nkeys * cfg.n_blocks * cfg.n_centroids * 24
+            extra["c3_encode_bf16"] = {"keys_per_s": nkeys / (ms_b * 1e-3), "ms": ms_b,
+                                       "hbm_gbs": nkeys * (cfg.head_dim * 2 + cfg.n_blocks) / (ms_b * 1e-3) / 1e9,
+                                       "argmin_compares_per_s": nkeys * cfg.n_blocks * cfg.n_centroids / (ms_b * 1e-3),
+                                       "tf32_tflops": flops / (ms_b * 1e-3) / 1e12,
+                                       "kernel": "encode_tc_kernel (tcgen05 kind::tf32, TMEM accumulator)"}
+            del kb
         del codec, idx, heavy, value, query, keys, out
         torch.cuda.empty_cache()
     return extra

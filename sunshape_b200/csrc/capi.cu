@@ -485,10 +485,20 @@ int sunshape_encode(const sunshape_codec_t* codec, const void* keys, int32_t key
   p.nb = D / bd; p.bd = bd; p.C = C; p.D = D;
   p.idx_out = indices_out; p.index_dtype = index_dtype; p.heavy_out = heavy_out; p.heavy_dtype = heavy_dtype;
   p.out_hs = out_head_stride;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // SUNSHAPE_ENCODE=cuda_cores forces the CUDA-core kernel (a cross-check of the tensor-core one)
+  const char* path = getenv("SUNSHAPE_ENCODE");
+  const bool force_cc = path && strcmp(path, "cuda_cores") == 0;
+  if (!force_cc && encode_tc_supported(p)) {
+    launch_encode_tc(p, n_heads, st);
+    return cuda_status("encode (tensor cores) launch");
+  }
+  if (path && strcmp(path, "tensor_cores") == 0)
+    return fail(SUNSHAPE_E_UNSUPPORTED, "SUNSHAPE_ENCODE=tensor_cores: needs bf16/f16 keys with 16-byte aligned rows, "
+                                        "block_dim 2, 4 or 8 and n_centroids a multiple of 16 up to 256.");
   const int smem = (kEncRows * (D + 1) + C * bd + C + D) * 4 + 64;
   if (smem > kSmemLimit) return fail(SUNSHAPE_E_UNSUPPORTED, "encode: codebook too large for shared memory.");
   dim3 grid((n_tokens + kEncRows - 1) / kEncRows, n_heads);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
 #define SUNSHAPE_ENC_CASE(B)                                                         \
   case B: {                                                                          \
     cudaFuncSetAttribute(encode_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \

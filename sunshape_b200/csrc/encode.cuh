@@ -11,27 +11,11 @@
 #pragma once
 
 #include "common.cuh"
+#include "encode_params.cuh"
 
 namespace sunshape {
 
-constexpr int kEncRows = 128;
 
-struct EncodeParams {
-  const void* keys;
-  int keys_dtype;
-  int64_t key_hs, key_ts;   // head / token strides (elements)
-  int n_tokens, kv_heads;
-  const float* cb;
-  int n_cb;
-  const int64_t* perm;
-  const uint8_t* heavy_mask;
-  int nb, bd, C, D;
-  void* idx_out;
-  int index_dtype;
-  void* heavy_out;
-  int heavy_dtype;
-  int64_t out_hs;           // output head stride (tokens)
-};
 
 template <int BD>
 __global__ void __launch_bounds__(kEncRows) encode_kernel(const __grid_constant__ EncodeParams p) {
