@@ -20,7 +20,10 @@ def fake_quantize_keys(codec, key_states: torch.Tensor) -> torch.Tensor:
     if key_states.ndim != 4:
         flat = key_states.reshape(1, 1, -1, key_states.shape[-1])
         return fake_quantize_keys(codec, flat).reshape(key_states.shape)
-    payload = quantize_codec_keys(codec, key_states.float())
+    # 16-bit keys go to the encoder as they are (exact in its tensor-core arithmetic; the reference
+    # upcasts them to fp32 first, cache.py:41-44, which holds the same values)
+    k = key_states if key_states.dtype in (torch.bfloat16, torch.float16) else key_states.float()
+    payload = quantize_codec_keys(codec, k)
     return dequantize_keys(codec, payload).to(key_states.dtype)
 
 

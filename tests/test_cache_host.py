@@ -1,0 +1,64 @@
+"""HF cache classes (reference ``sunshape/cache.py``): host-side plumbing on CPU.
+
+The quantize -> dequantize step itself runs on the GPU (covered by the encode and dequantize
+parity tests); here it is replaced by a marker function so the tests check what the cache does
+around it: which layers route keys through the codec, with which shapes and dtypes, that values
+are untouched and that sequences concatenate like ``DynamicLayer``.  Without the replacement, CPU
+keys must raise (there is no CPU fallback).
+"""
+import pytest
+import torch
+
+from sunshape_b200 import cache as cache_mod
+from sunshape_b200.cache import IdentityLayer, SunShapeCache, SunShapeLayer
+from sunshape_b200.codec import SunShapeBlockCodec
+from sunshape_b200.hf import SunShapeBundle
+
+
+def _codec():
+    return SunShapeBlockCodec(64, 8, 16, device=torch.device("cpu"))
+
+
+@pytest.fixture
+def marked(monkeypatch):
+    seen = []
+
+    def fake_quantize_keys(codec, key_states):
+        seen.append((codec, tuple(key_states.shape), key_states.dtype))
+        return key_states * 2
+
+    monkeypatch.setattr(cache_mod, "fake_quantize_keys", fake_quantize_keys)
+    return seen
+
+
+def test_codec_layers_quantize_keys_and_concatenate(marked):
+    codec = _codec()
+    cache = SunShapeCache(num_layers=3, layer_codecs={0: codec}, identity_layers={2})
+    assert [type(layer) for layer in cache.layers] == [SunShapeLayer, cache_mod.DynamicLayer, IdentityLayer]
+    k = torch.randn(2, 2, 5, 64, dtype=torch.bfloat16)
+    v = torch.randn(2, 2, 5, 64, dtype=torch.bfloat16)
+    k0, v0 = cache.update(k, v, 0)
+    assert torch.equal(k0, k * 2) and torch.equal(v0, v)
+    k0, v0 = cache.update(k[:, :, :1], v[:, :, :1], 0)      # one decode step appends
+    assert k0.shape == (2, 2, 6, 64) and torch.equal(k0[:, :, 5:], k[:, :, :1] * 2)
+    assert cache.get_seq_length(0) == 6
+    assert marked == [(codec, (2, 2, 5, 64), torch.bfloat16), (codec, (2, 2, 1, 64), torch.bfloat16)]
+    for layer_idx in (1, 2):                                 # plain and identity layers store keys as given
+        kk, vv = cache.update(k, v, layer_idx)
+        assert torch.equal(kk, k) and torch.equal(vv, v)
+    assert len(marked) == 2
+
+
+def test_bundle_cache_uses_bundle_codecs(marked):
+    codecs = {1: _codec(), 3: _codec()}
+    bundle = SunShapeBundle(model_name="m", layers=[1, 3], bits_per_dim=1.0, block_dim=8,
+                            mode="profileperm_baseline", cal_points=16, dsq_steps=3, seed=0, codecs=codecs)
+    cache = bundle.make_cache(num_layers=4)
+    assert [isinstance(layer, SunShapeLayer) for layer in cache.layers] == [False, True, False, True]
+    assert cache.layers[3].codec is codecs[3]
+
+
+def test_cpu_keys_have_no_fallback():
+    layer = SunShapeLayer(codec=_codec())
+    with pytest.raises(RuntimeError):
+        layer.update(torch.randn(1, 1, 3, 64), torch.randn(1, 1, 3, 64))
