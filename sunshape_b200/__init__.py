@@ -16,6 +16,9 @@ def __getattr__(name):
     if name in ("SunShapeCache", "SunShapeLayer", "IdentityLayer"):
         from . import cache
         return getattr(cache, name)
+    if name in ("TurboQuantCache", "TurboQuantLayer"):
+        from . import turbo_cache
+        return getattr(turbo_cache, name)
     if name in ("SunShapeBundle", "SunShapeCausalLM", "SunShapeConfig", "SunShapeForCausalLM", "TraceConfig",
                 "default_block_dim", "resolve_mode_alias"):
         from . import hf

@@ -13,6 +13,7 @@ from sunshape_b200 import cache as cache_mod
 from sunshape_b200.cache import IdentityLayer, SunShapeCache, SunShapeLayer
 from sunshape_b200.codec import SunShapeBlockCodec
 from sunshape_b200.hf import SunShapeBundle
+from sunshape_b200.turbo_cache import TurboQuantCache, TurboQuantLayer
 
 
 def _codec():
@@ -62,3 +63,24 @@ def test_cpu_keys_have_no_fallback():
     layer = SunShapeLayer(codec=_codec())
     with pytest.raises(RuntimeError):
         layer.update(torch.randn(1, 1, 3, 64), torch.randn(1, 1, 3, 64))
+
+
+def test_turbo_cache_routes_flattened_fp32_keys_through_quantizer():
+    seen = []
+
+    def quantizer(flat):
+        seen.append((tuple(flat.shape), flat.dtype))
+        return -flat
+
+    cache = TurboQuantCache.from_quantizers({1: quantizer}, num_layers=2)
+    assert [type(layer) for layer in cache.layers] == [cache_mod.DynamicLayer, TurboQuantLayer]
+    k = torch.randn(1, 2, 3, 64, dtype=torch.bfloat16)
+    v = torch.randn(1, 2, 3, 64, dtype=torch.bfloat16)
+    k1, v1 = cache.update(k, v, 1)
+    assert seen == [((6, 64), torch.float32)]
+    assert k1.dtype == torch.bfloat16 and torch.equal(k1, -k) and torch.equal(v1, v)
+    assert cache.get_seq_length(1) == 3 and not cache.has_previous_state()   # layer 0 decides, as in the reference
+    with pytest.raises(NotImplementedError):
+        TurboQuantCache.for_layers(head_dims={0: 64}, layers=[0], num_layers=1)
+    with pytest.raises(ValueError):
+        TurboQuantCache(num_layers=None)
