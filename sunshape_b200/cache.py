@@ -76,6 +76,14 @@ class SunShapeCache(DynamicCache):
         return cls(config=config, num_layers=num_layers, layer_codecs=codecs_dict)
 
     @classmethod
+    def from_traces(cls, traces: dict, layers: list[int], config=None, num_layers: int | None = None, **kwargs):
+        """Reference ``cache.py:131-186`` fits codecs from calibration traces; fitting is offline
+        calibration, not part of the decode path."""
+        raise NotImplementedError(
+            "SunShapeCache.from_traces fits codecs from traces (offline calibration); fit with the reference and "
+            "build the cache with SunShapeCache.from_codecs or SunShapeBundle.load(...).make_cache()")
+
+    @classmethod
     def identity(cls, patched_layers: list[int], config=None, num_layers: int | None = None) -> "SunShapeCache":
         return cls(config=config, num_layers=num_layers, identity_layers=set(patched_layers))
 

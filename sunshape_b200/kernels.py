@@ -50,6 +50,10 @@ def require_fast_path(codec, query: torch.Tensor, quantized_key) -> None:
         raise RuntimeError(reason)
 
 
+# the reference's public name for the same check (triton_kernels.py:366-373), kept for callers
+require_triton_fast_path = require_fast_path
+
+
 def _heavy_compact(codec: SunShapeBlockCodec, quantized_key) -> torch.Tensor | None:
     if not codec.is_mixed or getattr(quantized_key, "passthrough_blocks", None) is None:
         return None

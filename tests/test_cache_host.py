@@ -84,3 +84,11 @@ def test_turbo_cache_routes_flattened_fp32_keys_through_quantizer():
         TurboQuantCache.for_layers(head_dims={0: 64}, layers=[0], num_layers=1)
     with pytest.raises(ValueError):
         TurboQuantCache(num_layers=None)
+
+
+def test_reference_names_without_calibration_raise_with_reason():
+    from sunshape_b200.kernels import require_fast_path, require_triton_fast_path
+
+    assert require_triton_fast_path is require_fast_path
+    with pytest.raises(NotImplementedError, match="offline calibration"):
+        SunShapeCache.from_traces({}, [0], num_layers=1)
