@@ -148,3 +148,10 @@ class KVShardedDecode:
         return merge_gathered(gathered, (B, Hq, L, value.shape[-1]), value.dtype)
 
     __call__ = forward
+
+    def close(self) -> None:
+        """Unmap the peers' exchange buffers and free this rank's.  Every rank must have finished its
+        last decode first (a barrier), since peers store into this rank's buffer during a decode."""
+        for pg in self._peers.values():
+            pg.close()
+        self._peers.clear()
