@@ -361,7 +361,7 @@ def run_ours(args, cfg: DecodeConfig):
     alg = algorithmic_bytes(cfg, Tl)
     achieved = alg / (kernel_ms * 1e-3) / 1e9
     traffic = None
-    tp = os.path.join(ROOT, "profiles", f"decode_kernel_{cfg.name}.json")
+    tp = os.path.join(ROOT, "profiles", f"decode_mma_kernel_{cfg.name}_traffic.json")
     if os.path.exists(tp):
         # DRAM bytes per algorithmic byte from one ncu capture, applied to this launch's bytes
         with open(tp) as f:
