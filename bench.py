@@ -323,11 +323,10 @@ def run_ours(args, cfg: DecodeConfig):
     t_ms = e0.elapsed_time(e1) * args.steps / n_steps
     barrier()
     # e2e through the public API: pinned host query in, host output out, every step
-    from sunshape_b200.integration.vllm import SunShapeVLLMRuntimeState
+    from sunshape_b200.integration.vllm import runtime_state_from_bundle
     from sunshape_b200.hf import SunShapeBundle
     bundle = SunShapeBundle("synthetic", [0], 1.0, cfg.block_dim, "sunshape_base", 0, 0, 0, {0: codec}, {})
-    state = SunShapeVLLMRuntimeState("<memory>", "synthetic", "sunshape_base", 1.0, cfg.block_dim, [0], bundle,
-                                     str(dev))
+    state = runtime_state_from_bundle(bundle, device=str(dev))
     impl = vab.SunShapeAttentionImpl(layer_idx=0, runtime_state=state)
     q_host = query.cpu().pin_memory()
     o_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()

@@ -94,6 +94,12 @@ int sunshape_encode(const sunshape_codec_t* codec, const void* keys, int32_t key
                     void* heavy_out, int32_t heavy_dtype, int64_t out_head_stride,
                     void* stream);
 
+/* First device-side error code recorded by an encode kernel on the current device since the last
+ * clear (0 = none; 121 = a tensor-core completion wait gave up, the indices of that launch are
+ * invalid).  Waits for the device's queued work (cudaMemcpyFromSymbol); clear != 0 resets the word.
+ * No counterpart in the reference (its encode runs on the host). */
+int sunshape_encode_error(int32_t* code, int32_t clear);
+
 /* Dequantize into the model basis: out [n_heads, seq_len, head_dim] fp32. */
 int sunshape_dequantize(const sunshape_codec_t* codec, const sunshape_kv_t* kv,
                         int32_t n_heads, int32_t kv_heads, float* out, void* stream);
@@ -112,6 +118,13 @@ int sunshape_attention_scores(const sunshape_codec_t* codec, const sunshape_kv_t
  * stream order (calls that overlap on the GPU need separate workspaces). */
 int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_t rows,
                                         int32_t value_dim, int32_t n_blocks);
+
+/* Smallest workspace sunshape_decode_attention accepts for these sizes: the per-head LUTs are then
+ * built inside each CTA's shared memory instead of by a separate LUT kernel into the workspace.
+ * (sunshape_decode_workspace_bytes is the size that enables the LUT kernel; anything in between
+ * behaves like the minimum.)  No counterpart in the reference (it allocates per call). */
+int64_t sunshape_decode_workspace_min_bytes(int32_t n_heads, int32_t seq_len, int32_t rows,
+                                            int32_t value_dim);
 
 /* Fused quantized-key decode attention (LUT build + LUT-gather scores + online
  * softmax . V, split over the KV sequence inside the GPU).
@@ -172,10 +185,13 @@ int sunshape_decode_attention_peers(const sunshape_codec_t* codec, const sunshap
  * reserve all device memory up front and forbid allocation while decoding, and bindings with no
  * CUDA allocator of their own.  Arguments and results are those of sunshape_decode_attention;
  * the scratch is a fixed array of SUNSHAPE_NOALLOC_SCRATCH_BYTES compiled into the library (each
- * GPU that loads it keeps that much until the process exits).  Decodes whose workspace
- * (sunshape_decode_workspace_bytes) exceeds it are rejected with SUNSHAPE_E_WORKSPACE.
+ * GPU that loads it keeps that much until the process exits).  Decodes whose minimum workspace
+ * (sunshape_decode_workspace_min_bytes) exceeds it are rejected with SUNSHAPE_E_WORKSPACE; when
+ * the array is also large enough for the per-head LUT area (sunshape_decode_workspace_bytes) the
+ * decode uses it.  batch == 0 returns SUNSHAPE_OK without touching the device.
  * The first call on a device looks up the array's device address (with that device current), so
- * make that first call before any stream capture.  Every call clears the parts of the array that
+ * make that first call before any stream capture; the address is kept for the life of the process
+ * (do not call again after a cudaDeviceReset).  Every call clears the parts of the array that
  * must start at zero, on the given stream; all calls share the one array, so calls that can
  * overlap on the GPU (different streams, or different host threads) race and must be serialised
  * by the caller. */
@@ -186,6 +202,12 @@ int sunshape_decode_attention_noalloc(const sunshape_codec_t* codec, const sunsh
                                       int64_t mask_sb, int64_t mask_sh, int64_t mask_sq,
                                       float scale, void* out, int32_t out_dtype, float* partials,
                                       void* stream);
+
+/* Device-side error code of the last sunshape_decode_attention_noalloc call on the current device
+ * (0 = none; 101 / 102 = a bounded pipeline wait gave up and that call's output is invalid).  It
+ * lives at the start of the built-in array and stays readable until the next call clears it.
+ * Waits for the device's queued work (cudaMemcpyFromSymbol); allocates nothing. */
+int sunshape_decode_attention_noalloc_error(int32_t* code);
 
 /* Merge n_parts partial sets [n_parts, rows, 2 + value_dim] (as written by
  * sunshape_decode_attention) into out [rows, value_dim] of out_dtype:

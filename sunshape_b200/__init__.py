@@ -23,8 +23,7 @@ def __getattr__(name):
                 "default_block_dim", "resolve_mode_alias"):
         from . import hf
         return getattr(hf, name)
-    if name in ("SunShapeVLLMConfig", "SunShapeVLLMHandle", "SunShapeVLLMRuntimeState", "build_launch_env",
-                "load_runtime_state"):
+    if name in ("SunShapeVLLMHandle", "SunShapeVLLMRuntimeState", "load_runtime_state", "runtime_state_from_bundle"):
         from .integration import vllm
         return getattr(vllm, name)
     if name in ("SunShapeAttentionImpl", "SunShapeQuantizedKeys", "quantize_key_states"):

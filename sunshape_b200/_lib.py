@@ -29,7 +29,8 @@ EXPORTED_SYMBOLS = (
     "sunshape_attention_scores", "sunshape_decode_workspace_bytes", "sunshape_decode_attention",
     "sunshape_merge_partials", "sunshape_decode_attention_noalloc", "sunshape_peer_buffer_bytes",
     "sunshape_peer_alloc", "sunshape_peer_open", "sunshape_peer_close", "sunshape_peer_free",
-    "sunshape_decode_attention_peers",
+    "sunshape_decode_attention_peers", "sunshape_decode_workspace_min_bytes", "sunshape_encode_error",
+    "sunshape_decode_attention_noalloc_error",
 )
 
 
@@ -91,6 +92,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sunshape_decode_workspace_bytes.restype = ctypes.c_int64
         lib.sunshape_decode_attention.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64, i64,
                                                   f32, vp, i32, vp, vp, i64, vp]
+        lib.sunshape_decode_workspace_min_bytes.argtypes = [i32, i32, i32, i32]
+        lib.sunshape_decode_workspace_min_bytes.restype = ctypes.c_int64
+        lib.sunshape_encode_error.argtypes = [ctypes.POINTER(ctypes.c_int32), i32]
+        lib.sunshape_encode_error.restype = ctypes.c_int
+        lib.sunshape_decode_attention_noalloc_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+        lib.sunshape_decode_attention_noalloc_error.restype = ctypes.c_int
         lib.sunshape_merge_partials.argtypes = [vp, i32, i64, i32, vp, i32, vp]
         lib.sunshape_decode_attention_noalloc.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64,
                                                           i64, f32, vp, i32, vp, vp]
@@ -224,6 +231,19 @@ def decode_error_word(dev: torch.device | None = None) -> int:
     codes = [int(ws[:4].view(torch.int32).item()) for (d, _), ws in _workspaces.items()
              if dev is None or d == (dev.index or 0)]
     return next((c for c in codes if c), 0)
+
+
+def encode_error_word(dev: torch.device, clear: bool = True) -> int:
+    """Device error code recorded by the encode kernels on ``dev`` (0 = none); waits for the device."""
+    code = ctypes.c_int32(0)
+    with torch.cuda.device(dev):
+        _check(load_library().sunshape_encode_error(ctypes.byref(code), 1 if clear else 0))
+    return int(code.value)
+
+
+def decode_workspace_min_bytes(n_heads: int, seq_len: int, rows: int, value_dim: int) -> int:
+    """Smallest workspace the decode accepts (per-head LUTs built inside each CTA)."""
+    return int(load_library().sunshape_decode_workspace_min_bytes(n_heads, seq_len, rows, value_dim))
 
 
 def decode_attention(cd: CodecDesc, kd: KVDesc, query: torch.Tensor, batch: int, q_heads: int, kv_heads: int,

@@ -206,14 +206,29 @@ class SunShapeBlockCodec(torch.nn.Module):
             _lib.encode(desc, k, n_heads, kv_heads, T, k.stride(0), k.stride(1), idx, heavy, T)
         return idx, heavy
 
-    def quantize(self, keys: torch.Tensor, *, kv_head: int = 0) -> SunShapeQuantized:
-        """codec.py:362-385 for one head's keys [T, D] (``kv_head`` picks a per-head codebook)."""
+    def _require_head(self, kv_head: int | None, what: str) -> int | None:
+        """A codec holding one codebook per KV head needs to be told which head a call is for: the
+        reference signatures (one codec per layer) carry no head, and silently using codebook 0 for
+        every head would return wrong results without an error."""
+        if self.n_codebooks == 1:
+            return None
+        if kv_head is None:
+            raise RuntimeError(
+                f"{what}: this codec holds {self.n_codebooks} per-KV-head codebooks; pass kv_head= "
+                "(or use a one-codebook codec, as the reference does)")
+        if not 0 <= int(kv_head) < self.n_codebooks:
+            raise RuntimeError(f"{what}: kv_head {kv_head} out of range [0, {self.n_codebooks}).")
+        return int(kv_head)
+
+    def quantize(self, keys: torch.Tensor, *, kv_head: int | None = None) -> SunShapeQuantized:
+        """codec.py:362-385 for one head's keys [T, D] (``kv_head`` picks a per-head codebook and is
+        required when the codec holds more than one)."""
         keys = keys.to(self.device)
         if keys.dtype != torch.float32:
             keys = keys.float()
-        if self.n_codebooks > 1:
-            view = self._head_view(kv_head)
-            return view.quantize(keys)
+        h = self._require_head(kv_head, "quantize")
+        if h is not None:
+            return self._head_view(h).quantize(keys)
         idx, heavy = self.quantize_packed(keys.unsqueeze(0))
         idx = idx[0]
         pt_blocks = self.mixed_high_precision_blocks.detach().clone() if self.is_mixed else None
@@ -238,10 +253,11 @@ class SunShapeBlockCodec(torch.nn.Module):
             cache[kv_head] = v
         return v
 
-    def dequantize(self, quantized: SunShapeQuantized, *, kv_head: int = 0) -> torch.Tensor:
+    def dequantize(self, quantized: SunShapeQuantized, *, kv_head: int | None = None) -> torch.Tensor:
         """codec.py:387-398: [T, nb] indices (+ passthrough) -> [T, D] fp32 in the model basis."""
-        if self.n_codebooks > 1:
-            return self._head_view(kv_head).dequantize(quantized)
+        h = self._require_head(kv_head, "dequantize")
+        if h is not None:
+            return self._head_view(h).dequantize(quantized)
         desc, keep, n_heavy = self.kernel_desc()
         idx = quantized.indices
         if idx.dtype not in (torch.uint8, torch.int16, torch.int32):
@@ -259,14 +275,15 @@ class SunShapeBlockCodec(torch.nn.Module):
             _lib.dequantize(desc, kd, 1, 1, out)
         return out
 
-    def forward(self, keys: torch.Tensor) -> torch.Tensor:
-        return self.dequantize(self.quantize(keys))
+    def forward(self, keys: torch.Tensor, *, kv_head: int | None = None) -> torch.Tensor:
+        return self.dequantize(self.quantize(keys, kv_head=kv_head), kv_head=kv_head)
 
-    def attention_scores(self, query: torch.Tensor, quantized: SunShapeQuantized) -> torch.Tensor:
+    def attention_scores(self, query: torch.Tensor, quantized: SunShapeQuantized, *,
+                         kv_head: int | None = None) -> torch.Tensor:
         """codec.py:403-422 -- scores through the LUT kernel (no silent fallback)."""
         from .kernels import sunshape_attention_scores_strict
 
-        return sunshape_attention_scores_strict(self, query.to(self.device).float(), quantized)
+        return sunshape_attention_scores_strict(self, query.to(self.device).float(), quantized, kv_head=kv_head)
 
     def heldout_logit_mse(self, q_test: torch.Tensor, k_test: torch.Tensor) -> float:
         q_test = q_test.to(self.device).float()

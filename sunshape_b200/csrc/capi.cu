@@ -517,6 +517,14 @@ int sunshape_encode(const sunshape_codec_t* codec, const void* keys, int32_t key
   return cuda_status("encode launch");
 }
 
+int sunshape_encode_error(int32_t* code, int32_t clear) {
+  if (!code) return fail(SUNSHAPE_E_INVALID, "code pointer is NULL.");
+  const int e = encode_error_word(code, clear != 0);
+  if (e) return fail(SUNSHAPE_E_CUDA, std::string("reading the encode error word: ") +
+                                          cudaGetErrorString(static_cast<cudaError_t>(e)));
+  return SUNSHAPE_OK;
+}
+
 int sunshape_dequantize(const sunshape_codec_t* codec, const sunshape_kv_t* kv, int32_t n_heads, int32_t kv_heads,
                         float* out, void* stream) {
   if (int rc = check_codec(codec)) return rc;
@@ -604,6 +612,17 @@ int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_
   const int64_t lut_bytes = (int64_t)((std::max(n_blocks, 1) + 7) / 8) * 8 * kLutC * gp * 4;
   return mma_workspace_bytes(n_heads, grid, max_seg, gp, value_dim,
                              (int64_t)n_heads * lut_bytes <= kGlobalLutMaxBytes ? lut_bytes : 0);
+}
+
+int64_t sunshape_decode_workspace_min_bytes(int32_t n_heads, int32_t seq_len, int32_t rows, int32_t value_dim) {
+  if (n_heads <= 0 || seq_len <= 0 || rows <= 0) return 256;
+  const int gp = pick_gp(rows);
+  const int tph = (seq_len + kTileTokens - 1) / kTileTokens;
+  const int64_t total = (int64_t)n_heads * tph;
+  const int64_t grid = std::min<int64_t>(num_sms(), total);
+  const int64_t per_cta = (total + grid - 1) / grid;
+  const int64_t max_seg = (per_cta + tph - 1) / tph + 1;
+  return mma_workspace_bytes(n_heads, grid, max_seg, gp, value_dim, 0);
 }
 
 static int decode_impl(const sunshape_codec_t* codec, const sunshape_kv_t* kv, const void* query,

@@ -27,6 +27,10 @@
 
 namespace sunshape {
 
+// Error word of the encode kernels on this device (first writer wins; read and cleared by
+// sunshape_encode_error).  sunshape_encode has no workspace, so the word is library-global.
+__device__ int g_encode_error;
+
 namespace {
 
 constexpr int kTcRows = 128;          // keys per CTA = MMA M = TMEM lanes
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(kTcRows) encode_tc_kernel(const __grid_constan
         tc_mma_tf32(tmem, ad + 2 * k, bdsc + 2 * k, idesc, k > 0);
       tc_commit(bar);
     }
-    mbar_wait(bar, phase, p.err, 121);
+    mbar_wait(bar, phase, p.err ? p.err : &g_encode_error, 121);
     phase ^= 1u;
     tc_fence_after();
 
@@ -352,6 +356,15 @@ int launch_encode_tc(const EncodeParams& p, int n_heads, cudaStream_t st) {
       break;
   }
   return 0;
+}
+
+int encode_error_word(int* code, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_encode_error, sizeof(int), 0, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear && *code != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_encode_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice);
+  }
+  return e == cudaSuccess ? 0 : (int)e;
 }
 
 }  // namespace sunshape

@@ -28,7 +28,9 @@ constexpr int kMaxDevices = 128;
 void* g_scratch_addr[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
-// Resolve (once per device, with that device current) the device address of the array.
+// Resolve (once per device, with that device current) the device address of the array.  The address
+// is cached for the life of the process: after cudaDeviceReset the module is reloaded at a possibly
+// different address, so a process that resets a device must not call the entry point again.
 int scratch_for_current_device(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -57,14 +59,18 @@ extern "C" int sunshape_decode_attention_noalloc(
     int32_t q_heads, int32_t kv_heads, int32_t query_len, const void* mask, int32_t mask_dtype, int64_t mask_sb,
     int64_t mask_sh, int64_t mask_sq, float scale, void* out, int32_t out_dtype, float* partials, void* stream) {
   if (!kv) return sunshape::set_last_error(SUNSHAPE_E_INVALID, "KV descriptor is NULL.");
-  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || query_len <= 0 || q_heads % kv_heads != 0)
-    return sunshape::set_last_error(SUNSHAPE_E_INVALID, "batch / heads / query_len must be positive, q_heads a "
+  if (batch < 0 || q_heads <= 0 || kv_heads <= 0 || query_len <= 0 || q_heads % kv_heads != 0)
+    return sunshape::set_last_error(SUNSHAPE_E_INVALID, "batch must be >= 0, heads / query_len positive, q_heads a "
                                                         "multiple of kv_heads.");
+  if (batch == 0)   // nothing to decode: the regular entry point validates the rest and returns OK
+    return sunshape_decode_attention(codec, kv, query, query_dtype, batch, q_heads, kv_heads, query_len, mask,
+                                     mask_dtype, mask_sb, mask_sh, mask_sq, scale, out, out_dtype, partials, nullptr,
+                                     0, stream);
   const int32_t n_heads = batch * kv_heads;
-  if (!codec) return sunshape::set_last_error(SUNSHAPE_E_INVALID, "codec descriptor is NULL.");
-  if (codec->block_dim <= 0) return sunshape::set_last_error(SUNSHAPE_E_INVALID, "block_dim must be positive.");
-  const int64_t need = sunshape_decode_workspace_bytes(n_heads, kv->seq_len, (q_heads / kv_heads) * query_len,
-                                                       kv->value_dim, codec->head_dim / codec->block_dim);
+  // the smallest workspace the decode accepts (per-head LUTs then live in each CTA's shared memory); when
+  // the array also holds the LUT area, the decode uses it on its own
+  const int64_t need = sunshape_decode_workspace_min_bytes(n_heads, kv->seq_len, (q_heads / kv_heads) * query_len,
+                                                           kv->value_dim);
   if (need > (int64_t)SUNSHAPE_NOALLOC_SCRATCH_BYTES)
     return sunshape::set_last_error(
         SUNSHAPE_E_WORKSPACE,
@@ -83,4 +89,15 @@ extern "C" int sunshape_decode_attention_noalloc(
   return sunshape_decode_attention(codec, kv, query, query_dtype, batch, q_heads, kv_heads, query_len, mask, mask_dtype,
                                    mask_sb, mask_sh, mask_sq, scale, out, out_dtype, partials, scratch,
                                    (int64_t)SUNSHAPE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int sunshape_decode_attention_noalloc_error(int32_t* code) {
+  if (!code) return sunshape::set_last_error(SUNSHAPE_E_INVALID, "code pointer is NULL.");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(code, g_decode_scratch, sizeof(int32_t), 0, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess)
+    return sunshape::set_last_error(SUNSHAPE_E_CUDA,
+                                    (std::string("reading the decode scratch error word: ") + cudaGetErrorString(e)).c_str());
+  return SUNSHAPE_OK;
 }

@@ -1,114 +1,33 @@
-"""vLLM runtime state for the SunShape backend (reference ``sunshape/integration/vllm.py``).
+"""Runtime registry glue between a serving engine and the SunShape attention backend.
 
-Only the part the decode path consumes is behavioural: ``SunShapeVLLMRuntimeState.codec_for_layer``
-(reference ``:140-141``) hands the layer's codec to the attention backend.  The config / handle
-dataclasses keep the reference's fields so launch scripts written for it still work; real vLLM
-connector wiring is out of scope here, as it is in the reference (which only probes module names).
+The decode path needs one thing from the serving side: given a layer index, the codec
+that encoded that layer's keys.  The reference keeps it in a runtime-state object whose
+``codec_for_layer`` the attention backend calls (``sunshape/integration/vllm.py:127-141``,
+used at ``sunshape/vllm_attn_backend.py:108,295``).  This module provides that object,
+built from a bundle file or an in-memory bundle, and ``install_hooks``, which loads a
+bundle and registers it with the backend module in one call.
+
+Engine launch plumbing (connector configs, environment exports, engine-argument
+dictionaries) is not on the decode path and is not provided; an engine integration
+only needs ``load_runtime_state`` + ``register_runtime_state``.
 """
 from __future__ import annotations
 
 import importlib
-import json
-import os
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, fields
 from pathlib import Path
 from typing import Any, Iterable
 
 import torch
 
-DEFAULT_CONNECTOR_NAME = "sunshape"
 DEFAULT_BACKEND_MODULE = "sunshape_b200.vllm_attn_backend"
 
 
 @dataclass
-class SunShapeVLLMConfig:
-    model_name: str
-    bundle_path: str
-    mode: str
-    bits_per_dim: float
-    block_dim: int
-    layers: list[int]
-    connector_name: str = DEFAULT_CONNECTOR_NAME
-    backend_module: str = DEFAULT_BACKEND_MODULE
-    beta: bool = True
-
-    def runtime_entrypoint(self) -> str:
-        return f"{self.backend_module}:install_sunshape_hooks"
-
-    def launch_env(self) -> dict[str, str]:
-        return {
-            "SUNSHAPE_VLLM_CONNECTOR": self.connector_name,
-            "SUNSHAPE_VLLM_BUNDLE_PATH": self.bundle_path,
-            "SUNSHAPE_VLLM_MODE": self.mode,
-            "SUNSHAPE_VLLM_BITS_PER_DIM": str(self.bits_per_dim),
-            "SUNSHAPE_VLLM_BLOCK_DIM": str(self.block_dim),
-            "SUNSHAPE_VLLM_LAYERS": ",".join(str(x) for x in self.layers),
-            "SUNSHAPE_VLLM_BACKEND_MODULE": self.backend_module,
-        }
-
-    def engine_args(self) -> dict[str, Any]:
-        return {
-            "model": self.model_name,
-            "kv_transfer_config": {"connector": self.connector_name, "bundle_path": self.bundle_path,
-                                   "mode": self.mode, "bits_per_dim": self.bits_per_dim,
-                                   "block_dim": self.block_dim, "layers": list(self.layers)},
-            "sunshape_runtime": {"backend_module": self.backend_module,
-                                 "install_entrypoint": self.runtime_entrypoint(), "beta": self.beta},
-        }
-
-    def to_dict(self) -> dict[str, Any]:
-        return {"model_name": self.model_name, "bundle_path": self.bundle_path, "mode": self.mode,
-                "bits_per_dim": self.bits_per_dim, "block_dim": self.block_dim, "layers": list(self.layers),
-                "connector_name": self.connector_name, "backend_module": self.backend_module, "beta": self.beta,
-                "engine_args": self.engine_args(), "launch_env": self.launch_env()}
-
-    def save_json(self, path: str | Path) -> Path:
-        path = Path(path)
-        path.parent.mkdir(parents=True, exist_ok=True)
-        path.write_text(json.dumps(self.to_dict(), indent=2))
-        return path
-
-
-@dataclass
-class SunShapeVLLMHandle:
-    config: SunShapeVLLMConfig
-    hooks_installed: bool
-    backend_module: str | None = None
-    connector_registered: bool = False
-    runtime_patch_available: bool = False
-    vllm_version: str | None = None
-    notes: list[str] = field(default_factory=list)
-
-    def engine_args(self) -> dict[str, Any]:
-        return self.config.engine_args()
-
-    def to_dict(self) -> dict[str, Any]:
-        return {"config": self.config.to_dict(), "hooks_installed": self.hooks_installed,
-                "backend_module": self.backend_module, "connector_registered": self.connector_registered,
-                "runtime_patch_available": self.runtime_patch_available, "vllm_version": self.vllm_version,
-                "notes": list(self.notes)}
-
-    def activate(self) -> "SunShapeVLLMHandle":
-        backend = importlib.import_module(self.backend_module or self.config.backend_module)
-        if hasattr(backend, "register_handle"):
-            backend.register_handle(self)
-            self.hooks_installed = True
-            self.connector_registered = True
-        return self
-
-    def deactivate(self) -> "SunShapeVLLMHandle":
-        backend = importlib.import_module(self.backend_module or self.config.backend_module)
-        if hasattr(backend, "clear_registered_runtime"):
-            backend.clear_registered_runtime()
-        if hasattr(backend, "clear_registered_handle"):
-            backend.clear_registered_handle()
-        self.hooks_installed = False
-        self.connector_registered = False
-        return self
-
-
-@dataclass
 class SunShapeVLLMRuntimeState:
+    """Per-process codec registry.  Field names follow the reference's runtime state so code that
+    builds one by keyword keeps working; ``bundle`` is a ``sunshape_b200.hf.SunShapeBundle``."""
+
     bundle_path: str
     model_name: str
     mode: str
@@ -121,64 +40,82 @@ class SunShapeVLLMRuntimeState:
     beta: bool = True
 
     def codec_for_layer(self, layer_idx: int):
+        """The layer's codec, or None when the layer is not quantized."""
         return self.bundle.codecs.get(int(layer_idx))
 
     def supports_layer(self, layer_idx: int) -> bool:
-        return int(layer_idx) in self.bundle.codecs
+        return self.codec_for_layer(layer_idx) is not None
 
     def to_dict(self) -> dict[str, Any]:
-        return {"bundle_path": self.bundle_path, "model_name": self.model_name, "mode": self.mode,
-                "bits_per_dim": self.bits_per_dim, "block_dim": self.block_dim, "layers": list(self.layers),
-                "device": self.device, "backend_module": self.backend_module, "beta": self.beta,
-                "trace_meta": dict(getattr(self.bundle, "trace_meta", {}))}
+        d = {f.name: getattr(self, f.name) for f in fields(self) if f.name != "bundle"}
+        d["layers"] = [int(x) for x in self.layers]
+        d["trace_meta"] = dict(getattr(self.bundle, "trace_meta", {}) or {})
+        return d
 
 
 def runtime_state_from_bundle(bundle, *, bundle_path: str = "<memory>", device: str | None = None,
                               layers: Iterable[int] | None = None) -> SunShapeVLLMRuntimeState:
     """Runtime state around an in-memory bundle (no file round trip)."""
+    if device is None:
+        first = next(iter(bundle.codecs.values()), None)
+        device = str(first.device) if first is not None else "cuda"
     return SunShapeVLLMRuntimeState(
         bundle_path=str(bundle_path), model_name=bundle.model_name, mode=bundle.mode,
         bits_per_dim=float(bundle.bits_per_dim), block_dim=int(bundle.block_dim),
-        layers=[int(x) for x in layers] if layers else list(bundle.layers), bundle=bundle,
-        device=str(device or next(iter(bundle.codecs.values())).device if bundle.codecs else "cuda"))
+        layers=sorted(int(x) for x in (layers if layers else bundle.layers)), bundle=bundle, device=str(device))
 
 
 def load_runtime_state(*, bundle_path: str | Path, model_name: str, mode: str, bits_per_dim: float,
                        block_dim: int, layers: Iterable[int], backend_module: str = DEFAULT_BACKEND_MODULE,
                        device: str | torch.device | None = None) -> SunShapeVLLMRuntimeState:
+    """Load a bundle file (the reference's format) onto ``device`` (default: the current CUDA device)."""
     from ..hf import SunShapeBundle
 
-    bundle_path = Path(bundle_path)
-    if not bundle_path.exists():
-        raise FileNotFoundError(f"SunShape vLLM bundle does not exist: {bundle_path}")
+    path = Path(bundle_path)
+    if not path.is_file():
+        raise FileNotFoundError(f"SunShape vLLM bundle does not exist: {path}")
     dev = torch.device(device) if device is not None else torch.device("cuda")
-    bundle = SunShapeBundle.load(bundle_path, device=dev)
-    return SunShapeVLLMRuntimeState(
-        bundle_path=str(bundle_path), model_name=model_name, mode=mode, bits_per_dim=float(bits_per_dim),
-        block_dim=int(block_dim), layers=[int(x) for x in layers] if layers else list(bundle.layers),
-        bundle=bundle, device=str(dev), backend_module=backend_module, beta=True)
+    bundle = SunShapeBundle.load(path, device=dev)
+    state = runtime_state_from_bundle(bundle, bundle_path=str(path), device=str(dev), layers=layers)
+    state.model_name, state.mode = model_name, mode
+    state.bits_per_dim, state.block_dim = float(bits_per_dim), int(block_dim)
+    state.backend_module = backend_module
+    return state
 
 
-def build_launch_env(config: SunShapeVLLMConfig) -> dict[str, str]:
-    env = dict(config.launch_env())
-    env["VLLM_ATTENTION_BACKEND"] = config.connector_name
-    env["SUNSHAPE_VLLM_INSTALL_ENTRYPOINT"] = config.runtime_entrypoint()
-    return env
+@dataclass
+class SunShapeVLLMHandle:
+    """What ``install_hooks`` returns: the registered state and where it was registered."""
+
+    state: SunShapeVLLMRuntimeState
+    backend_module: str = DEFAULT_BACKEND_MODULE
+    hooks_installed: bool = False
+    notes: list[str] = field(default_factory=list)
+
+    def to_dict(self) -> dict[str, Any]:
+        return {"backend_module": self.backend_module, "hooks_installed": self.hooks_installed,
+                "notes": list(self.notes), "runtime": self.state.to_dict()}
+
+    def deactivate(self) -> "SunShapeVLLMHandle":
+        backend = importlib.import_module(self.backend_module)
+        backend.clear_registered_runtime()
+        backend.clear_registered_handle()
+        self.hooks_installed = False
+        return self
 
 
 def install_hooks(*, bundle_path: str | Path, model_name: str, mode: str, bits_per_dim: float, block_dim: int,
-                  layers: Iterable[int]) -> SunShapeVLLMHandle:
-    """Register the runtime state with the backend module (vLLM itself is optional here)."""
-    config = SunShapeVLLMConfig(model_name=model_name, bundle_path=str(bundle_path), mode=mode,
-                                bits_per_dim=float(bits_per_dim), block_dim=int(block_dim),
-                                layers=[int(x) for x in layers])
-    handle = SunShapeVLLMHandle(config=config, hooks_installed=False, backend_module=config.backend_module)
-    handle.activate()
-    backend = importlib.import_module(config.backend_module)
+                  layers: Iterable[int], backend_module: str = DEFAULT_BACKEND_MODULE,
+                  device: str | torch.device | None = None) -> SunShapeVLLMHandle:
+    """Load the bundle and register it (and the returned handle) with the backend module, so
+    ``SunShapeAttentionImpl`` / ``quantize_key_states`` find the codecs by layer index."""
     state = load_runtime_state(bundle_path=bundle_path, model_name=model_name, mode=mode,
                                bits_per_dim=bits_per_dim, block_dim=block_dim, layers=layers,
-                               backend_module=config.backend_module)
+                               backend_module=backend_module, device=device)
+    backend = importlib.import_module(backend_module)
+    handle = SunShapeVLLMHandle(state=state, backend_module=backend_module)
     backend.register_runtime_state(state)
-    os.environ["VLLM_ATTENTION_BACKEND"] = config.connector_name
-    handle.notes.append("Registered SunShape runtime state for the B200 attention backend.")
+    backend.register_handle(handle)
+    handle.hooks_installed = True
+    handle.notes.append(f"runtime state for layers {state.layers} registered with {backend_module}")
     return handle

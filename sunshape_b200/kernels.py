@@ -65,11 +65,15 @@ def _heavy_compact(codec: SunShapeBlockCodec, quantized_key) -> torch.Tensor | N
     return pv[:, codec.heavy_block_ids()].float().contiguous()
 
 
-def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, *, kv_head: int = 0) -> torch.Tensor:
-    """Scores [num_query_heads, num_tokens] fp32 on the B200 kernel, or raise."""
+def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, *,
+                                     kv_head: int | None = None) -> torch.Tensor:
+    """Scores [num_query_heads, num_tokens] fp32 on the B200 kernel, or raise.
+
+    ``kv_head`` selects the codebook of a per-KV-head codec and is required for one."""
     require_fast_path(codec, query, quantized_key)
-    if codec.n_codebooks > 1:
-        codec = codec._head_view(kv_head)
+    h = codec._require_head(kv_head, "sunshape_attention_scores")
+    if h is not None:
+        codec = codec._head_view(h)
     desc, keep, n_heavy = codec.kernel_desc()
     idx = quantized_key.indices
     if idx.dtype != torch.uint8:
@@ -90,14 +94,14 @@ def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, 
     return out
 
 
-def sunshape_attention_scores(codec, query: torch.Tensor, quantized_key) -> torch.Tensor:
+def sunshape_attention_scores(codec, query: torch.Tensor, quantized_key, *, kv_head: int | None = None) -> torch.Tensor:
     """``<query, k_hat>`` against block-quantized keys (triton_kernels.py:570-609), on the B200 kernel."""
-    return sunshape_attention_scores_strict(codec, query, quantized_key)
+    return sunshape_attention_scores_strict(codec, query, quantized_key, kv_head=kv_head)
 
 
-def _torch_attention_scores(codec, query: torch.Tensor, quantized_key) -> torch.Tensor:
+def _torch_attention_scores(codec, query: torch.Tensor, quantized_key, *, kv_head: int | None = None) -> torch.Tensor:
     """Dequantize-then-matmul reference path (triton_kernels.py:300-311), dequantize on the GPU kernel."""
-    k_hat = codec.dequantize(quantized_key)
+    k_hat = codec.dequantize(quantized_key, kv_head=kv_head)
     return torch.matmul(query.float(), k_hat.float().transpose(-2, -1))
 
 

@@ -25,7 +25,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .codec import SunShapeQuantized
-from .integration.vllm import SunShapeVLLMConfig, SunShapeVLLMHandle, SunShapeVLLMRuntimeState, install_hooks
+from .integration.vllm import SunShapeVLLMHandle, SunShapeVLLMRuntimeState, install_hooks
 
 MODE_ACTIVE = "active"
 MODE_CAPTURE = "capture"
@@ -161,6 +161,10 @@ def _decode_keys_if_needed(layer_idx: int | None, key_states: torch.Tensor) -> t
     codec = runtime.codec_for_layer(int(layer_idx))
     if codec is None or key_states.ndim < 2:
         return key_states
+    if key_states.ndim == 4:      # [B, Hkv, S, D]: one launch each way, per-KV-head codebooks included
+        from .cache import fake_quantize_keys
+
+        return fake_quantize_keys(codec, key_states)
     orig_shape, orig_dtype = key_states.shape, key_states.dtype
     decoded = codec(key_states.reshape(-1, orig_shape[-1]).float())
     return decoded.to(orig_dtype).reshape(orig_shape)
@@ -436,24 +440,19 @@ def describe_backend() -> dict[str, Any]:
     handle = get_registered_handle()
     if handle is None:
         return {"mode": get_mode(), "registered": False, "config": None, "runtime": None}
-    return {
-        "mode": get_mode(),
-        "registered": True,
-        "config": handle.config.to_dict(),
-        "hooks_installed": handle.hooks_installed,
-        "connector_registered": handle.connector_registered,
-        "runtime_patch_available": handle.runtime_patch_available,
-        "notes": list(handle.notes),
-        "runtime": _RUNTIME_STATE.to_dict() if _RUNTIME_STATE is not None else None,
-    }
+    d = {"mode": get_mode(), "registered": True}
+    d.update(handle.to_dict())
+    d["runtime"] = _RUNTIME_STATE.to_dict() if _RUNTIME_STATE is not None else None
+    return d
 
 
 def install_sunshape_hooks(*args, **kwargs) -> SunShapeVLLMHandle:
-    return register_handle(install_hooks(*args, **kwargs))
+    """Load a bundle and register its codecs with this backend (``integration.vllm.install_hooks``)."""
+    return install_hooks(*args, backend_module=__name__, **kwargs)
 
 
 __all__ = [
-    "MODE_ACTIVE", "MODE_CAPTURE", "MODE_OFF", "SunShapeVLLMConfig", "SunShapeVLLMHandle",
+    "MODE_ACTIVE", "MODE_CAPTURE", "MODE_OFF", "SunShapeVLLMHandle",
     "SunShapeVLLMRuntimeState", "SunShapeAttentionBackend", "SunShapeAttentionImpl", "SunShapeQuantizedKeys",
     "clear_registered_handle", "clear_registered_runtime", "describe_backend", "ensure_backend_registered",
     "get_mode", "get_registered_handle", "get_registered_runtime", "get_backend_factory", "install_sunshape_hooks",

@@ -12,6 +12,9 @@ heads), and records the reference's own outputs:
 * ``codec.quantize`` indices / passthrough      (codec.py:362-385)
 * ``_torch_attention_scores`` per head           (triton_kernels.py:300-311)
 * ``_apply_quantized_attention`` output          (vllm_attn_backend.py:216-253)
+* a bundle saved by ``SunShapeBundle.save`` and the decode of its layers through
+  ``SunShapeAttentionImpl.forward`` (``bundle_ref.pt``, ``g7_bundle.npz``)
+* the keys and values ``SunShapeCache.update`` stores over prefill + decode (``g8_cache.npz``)
 
 The results are written to ``tests/golden/<case>.npz`` together with the inputs,
 so tests never need the reference at run time.
@@ -138,8 +141,100 @@ def run_case(name, spec):
     print(f"{name}: wrote {os.path.getsize(path) / 1024:.0f} KiB")
 
 
+def _ref_codec(cfg, case, mode):
+    """A reference codec (one codebook shared by all KV heads, the reference's layout) with its
+    buffers written from the seeded case: codebook of KV head 0."""
+    from sunshape.codec import SunShapeBlockCodec
+
+    codec = SunShapeBlockCodec(head_dim=cfg.head_dim, block_dim=cfg.block_dim, n_centroids=cfg.n_centroids,
+                               mode=mode, device=torch.device("cpu"))
+    codec.permutation.copy_(case["perm"])
+    codec.inv_permutation.copy_(case["inv_perm"])
+    codec.centroids.copy_(case["centroids"][0])
+    codec.mixed_high_precision_blocks.copy_(case["heavy_mask"])
+    return codec
+
+
+def run_bundle():
+    """A bundle written by the reference's SunShapeBundle.save (hf.py:273-303) with two layers -- one
+    SunShape-base, one SunShape-Mixed -- plus, per layer, the reference's decode through its public
+    backend: runtime registry -> SunShapeAttentionImpl.forward (vllm_attn_backend.py:271-305) on keys
+    quantized by quantize_key_states (:101-123)."""
+    from sunshape import vllm_attn_backend as rb
+    from sunshape.hf import SunShapeBundle
+    from sunshape.integration.vllm import SunShapeVLLMRuntimeState
+
+    layer_cfgs = {3: (CONFIGS["c2"].with_(batch=2, q_heads=8, kv_heads=2, seq_len=300), "profileperm_baseline"),
+                  5: (CONFIGS["c4"].with_(batch=1, q_heads=8, kv_heads=2, seq_len=200), "profileperm_mixed_precision")}
+    codecs, cases = {}, {}
+    for layer, (cfg, mode) in layer_cfgs.items():
+        case = make_case(cfg, device="cpu", seed=40 + layer)
+        codecs[layer] = _ref_codec(cfg, case, mode)
+        cases[layer] = (cfg, case)
+    bundle = SunShapeBundle(model_name="synthetic-ref", layers=sorted(codecs), bits_per_dim=1.0, block_dim=8,
+                            mode="sunshape_base", cal_points=256, dsq_steps=0, seed=0, codecs=codecs,
+                            trace_meta={"source": "make_golden.py"})
+    bpath = os.path.join(HERE, "bundle_ref.pt")
+    bundle.save(bpath)
+    state = SunShapeVLLMRuntimeState(bundle_path=bpath, model_name="synthetic-ref", mode="sunshape_base",
+                                     bits_per_dim=1.0, block_dim=8, layers=sorted(codecs), bundle=bundle,
+                                     device="cpu")
+    rb.register_runtime_state(state)
+    payload = {}
+    for layer, (cfg, case) in cases.items():
+        keys = case["keys"]
+        if cfg.dtype != "f32":
+            keys = keys.to(cfg.torch_dtype)        # a model hands 16-bit keys to the backend
+        qk = rb.quantize_key_states(layer, keys)
+        impl = rb.SunShapeAttentionImpl(layer_idx=layer, runtime_state=state)
+        out = impl.forward(case["query"], qk, case["value"], scale=case["scale"])
+        idx = np.stack([h.indices.numpy() for h in qk.quantized_heads]).reshape(cfg.batch, cfg.kv_heads,
+                                                                                cfg.seq_len, -1)
+        pre = f"l{layer}_"
+        payload.update({pre + "keys": keys.float().numpy(), pre + "query": case["query"].float().numpy(),
+                        pre + "value": case["value"].float().numpy(), pre + "scale": np.float64(case["scale"]),
+                        pre + "dtype": cfg.dtype, pre + "ref_indices": idx.astype(np.uint8),
+                        pre + "ref_out": out.float().numpy()})
+    rb.clear_registered_runtime()
+    path = os.path.join(HERE, "g7_bundle.npz")
+    np.savez_compressed(path, layers=np.array(sorted(cases)), **payload)
+    print(f"bundle_ref.pt: {os.path.getsize(bpath) / 1024:.0f} KiB; g7_bundle: {os.path.getsize(path) / 1024:.0f} KiB")
+
+
+def run_cache():
+    """The reference's HF cache (cache.py:32-46, 55-104): a prefill of 37 bf16 keys then two decode
+    steps through SunShapeCache.update on layer 1 (layer 0 unquantized); records what the cache
+    stores (the fake-quantized keys and the values) after every update."""
+    from sunshape.cache import SunShapeCache
+
+    cfg = CONFIGS["c2"].with_(batch=2, q_heads=8, kv_heads=2, head_dim=64, seq_len=39)
+    case = make_case(cfg, device="cpu", seed=61)
+    codec = _ref_codec(cfg, case, "profileperm_baseline")
+    cache = SunShapeCache.from_codecs({1: codec}, num_layers=2)
+    keys = case["keys"].to(torch.bfloat16)
+    vals = case["value"]
+    steps = [(0, 37), (37, 38), (38, 39)]
+    payload = {"keys": keys.float().numpy(), "value": vals.float().numpy(), "perm": case["perm"].numpy(),
+               "inv_perm": case["inv_perm"].numpy(), "centroids": case["centroids"][0].numpy(),
+               "steps": np.array(steps)}
+    for i, (a, b) in enumerate(steps):
+        for layer in (0, 1):
+            k_out, v_out = cache.update(keys[:, :, a:b], vals[:, :, a:b], layer)
+            payload[f"step{i}_l{layer}_keys"] = k_out.float().numpy()
+            payload[f"step{i}_l{layer}_values"] = v_out.float().numpy()
+    path = os.path.join(HERE, "g8_cache.npz")
+    np.savez_compressed(path, **payload)
+    print(f"g8_cache: wrote {os.path.getsize(path) / 1024:.0f} KiB")
+
+
 if __name__ == "__main__":
     import sunshape  # noqa: F401  (must resolve to the reference checkout)
+    which = set(sys.argv[1:])
     torch.manual_seed(0)
     for n, s in CASES.items():
-        run_case(n, s)
+        if not which or n in which:
+            run_case(n, s)
+    if not which or "bundle" in which:
+        run_bundle()
+    if not which or "cache" in which:
+        run_cache()

@@ -8,7 +8,10 @@ import numpy as np
 import torch
 
 GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-GOLDEN_CASES = sorted(os.path.splitext(os.path.basename(p))[0] for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+# per-case decode fixtures; g7_bundle (reference bundle decode) and g8_cache (reference HF cache) have their own tests
+GOLDEN_CASES = sorted(n for n in (os.path.splitext(os.path.basename(p))[0]
+                                  for p in glob.glob(os.path.join(GOLDEN_DIR, "*.npz")))
+                      if n not in ("g7_bundle", "g8_cache"))
 
 # tolerances stated by the north star: fp32 accumulation rel 1e-5, bf16 outputs 2e-2
 TOL_F32 = 1e-5
@@ -51,15 +54,23 @@ def make_codec(perm, centroids, heavy_mask, head_dim, block_dim, n_centroids, de
     return codec
 
 
-def assert_close_normwise(actual, expected, rtol, what=""):
+def assert_close_rowwise(actual, expected, rtol, what=""):
+    """Per-row tolerance: for every row (the last axis: one output row of one query head, or one
+    score row), max |actual - expected| <= rtol * max |expected| over that row.  NaN patterns
+    (fully masked rows) must agree exactly."""
     a = np.asarray(actual, dtype=np.float64)
     e = np.asarray(expected, dtype=np.float64)
     assert a.shape == e.shape, (a.shape, e.shape)
     nan_a, nan_e = np.isnan(a), np.isnan(e)
     assert (nan_a == nan_e).all(), f"{what}: NaN pattern differs ({nan_a.sum()} vs {nan_e.sum()})"
-    fin = ~nan_e
-    if not fin.any():
+    if e.size == 0:
         return
-    scale = max(np.abs(e[fin]).max(), 1e-30)
-    err = np.abs(a[fin] - e[fin]).max()
-    assert err <= rtol * scale, f"{what}: max err {err:.3e} > {rtol:.1e} * {scale:.3e}"
+    a2 = np.where(nan_e, 0.0, a).reshape(-1, e.shape[-1])
+    e2 = np.where(nan_e, 0.0, e).reshape(-1, e.shape[-1])
+    scale = np.maximum(np.abs(e2).max(axis=1), 1e-30)
+    err = np.abs(a2 - e2).max(axis=1)
+    bad = err > rtol * scale
+    if bad.any():
+        r = int(np.argmax(err / scale))
+        raise AssertionError(f"{what}: {int(bad.sum())} of {len(bad)} rows out of tolerance; worst row {r}: "
+                             f"max err {err[r]:.3e} > {rtol:.1e} * {scale[r]:.3e}")

@@ -73,3 +73,27 @@ def test_cpu_tensors_raise_no_fallback():
                        "cpu")
     with pytest.raises(RuntimeError, match="CUDA"):
         codec.quantize(torch.randn(10, 64))
+
+
+def test_per_head_codec_requires_kv_head():
+    """The reference signatures carry no KV head; on a codec with one codebook per KV head they must
+    raise instead of silently using codebook 0 for every head."""
+    import torch
+
+    from sunshape_b200.kernels import sunshape_attention_scores
+    from tests.helpers import make_codec
+
+    codec = make_codec(torch.arange(64), torch.zeros(2, 8, 256, 8), torch.zeros(8, dtype=torch.bool), 64, 8, 256,
+                       "cpu")
+    with pytest.raises(RuntimeError, match="kv_head"):
+        codec.quantize(torch.randn(10, 64))
+    with pytest.raises(RuntimeError, match="kv_head"):
+        codec.dequantize(None)
+    with pytest.raises(RuntimeError, match="out of range"):
+        codec.quantize(torch.randn(10, 64), kv_head=2)
+
+    class _QK:
+        indices = torch.zeros(10, 8, dtype=torch.uint8)
+
+    with pytest.raises(RuntimeError, match="kv_head|CUDA"):
+        sunshape_attention_scores(codec, torch.randn(4, 64), _QK())

@@ -51,7 +51,8 @@ def _worker(rank, world, port, q):
                     codec=codec, query=qry, key=qk, value=case["value"], attn_mask=None,
                     scale=case["scale"]).float().cpu().numpy()
                 out = dec(qry, shard, v, scale=case["scale"]).float().cpu().numpy()
-                worst = max(worst, float(np.abs(out - ref).max() / np.abs(ref).max()))
+                rows_err = np.abs(out - ref).reshape(-1, ref.shape[-1]).max(1) / np.abs(ref).reshape(-1, ref.shape[-1]).max(1)
+                worst = max(worst, float(rows_err.max()))
             errs[mode] = worst
         torch.cuda.synchronize()
         q.put((rank, "ok", errs))
@@ -76,4 +77,4 @@ def test_kv_split_two_gpus_peer_and_nccl_match_single_gpu():
     for rank, status, val in res:
         assert status == "ok", val
         for mode, err in val.items():
-            assert err <= 2e-2, f"rank {rank} {mode}: normwise error {err:.3e}"
+            assert err <= 2e-2, f"rank {rank} {mode}: worst per-row error {err:.3e}"

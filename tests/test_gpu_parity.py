@@ -5,9 +5,9 @@ import torch
 
 from oracle import sunshape_oracle as O
 from sunshape_b200 import vllm_attn_backend as vab
-from sunshape_b200.kernels import sunshape_attention_scores
+from sunshape_b200.kernels import _torch_attention_scores, sunshape_attention_scores
 from sunshape_b200.workloads import CONFIGS, make_case
-from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_normwise, load_golden, make_codec, torch_dtype
+from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_rowwise, load_golden, make_codec, torch_dtype
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -63,7 +63,7 @@ def test_decode_matches_reference_output(name):
     torch.cuda.synchronize()
     assert out.dtype == dt and out.shape == (g["B"], g["Hq"], g["L"], g["D"])
     tol = TOL_F32 if g["dtype"] == "f32" else TOL_BF16
-    assert_close_normwise(out.float().cpu().numpy(), g["ref_out"], tol, f"{name} decode")
+    assert_close_rowwise(out.float().cpu().numpy(), g["ref_out"], tol, f"{name} decode")
 
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
@@ -78,8 +78,19 @@ def test_scores_match_reference(name):
             q = torch.from_numpy(g["query"][b, h * G:(h + 1) * G]).to(DEV).to(dt)
             if g["scale"] is not None:
                 q = q * float(g["scale"])
-            s = sunshape_attention_scores(codec._head_view(h), q.reshape(-1, g["D"]), keys.head(b, h))
-            assert_close_normwise(s.cpu().numpy(), g["ref_scores"][b, h], TOL_F32, f"{name} scores b{b}h{h}")
+            qh, kh = q.reshape(-1, g["D"]), keys.head(b, h)
+            ref = g["ref_scores"][b, h]
+            s = sunshape_attention_scores(codec, qh, kh, kv_head=h)
+            assert_close_rowwise(s.cpu().numpy(), ref, TOL_F32, f"{name} scores b{b}h{h}")
+            # the codec method (codec.py:403-422) upcasts the query to fp32 first, as the reference does
+            s2 = codec.attention_scores(qh, kh, kv_head=h)
+            assert_close_rowwise(s2.cpu().numpy(), ref, TOL_F32, f"{name} codec.attention_scores b{b}h{h}")
+            # dequantize + cuBLAS matmul (triton_kernels.py:300-311)
+            s3 = _torch_attention_scores(codec, qh, kh, kv_head=h)
+            assert_close_rowwise(s3.cpu().numpy(), ref, TOL_F32, f"{name} _torch_attention_scores b{b}h{h}")
+    if g["Hkv"] > 1:
+        with pytest.raises(RuntimeError, match="kv_head"):
+            sunshape_attention_scores(codec, torch.zeros(1, g["D"], device=DEV), keys.head(0, 0))
 
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
@@ -154,7 +165,48 @@ def test_decode_matches_oracle_seeded(name):
                                          attn_mask=mask, scale=scale)
     ref = _oracle_out(case, qk.indices, qk.heavy, mask, scale)
     tol = TOL_F32 if cfg.dtype == "f32" else TOL_BF16
-    assert_close_normwise(out.float().cpu().numpy(), ref, tol, name)
+    assert_close_rowwise(out.float().cpu().numpy(), ref, tol, name)
+
+
+# The in-CTA LUT branch: with the smallest accepted workspace (no room for the per-head LUT area),
+# every CTA builds its heads' LUTs in shared memory instead of the separate LUT kernel.
+MIN_WS = {
+    "c5_g8_fp16lut": CONFIGS["c5"].with_(batch=2, kv_heads=2, q_heads=16, seq_len=20000),
+    "c3_nb32": CONFIGS["c3"].with_(batch=1, kv_heads=2, q_heads=8, seq_len=9000),
+    "c2_g4": CONFIGS["c2"].with_(batch=3, kv_heads=2, q_heads=8, seq_len=7000 + 3),
+    "c4_mixed": CONFIGS["c4"].with_(batch=1, kv_heads=2, q_heads=8, seq_len=5000),
+}
+
+
+@pytest.mark.parametrize("name", list(MIN_WS))
+def test_decode_in_cta_lut_with_minimum_workspace(name):
+    from sunshape_b200 import _lib
+
+    cfg = MIN_WS[name]
+    case = make_case(cfg, device=DEV, seed=23)
+    codec = make_codec(case["perm"], case["centroids"], case["heavy_mask"], cfg.head_dim, cfg.block_dim,
+                       cfg.n_centroids, DEV)
+    qk = vab.quantize_codec_keys(codec, case["keys"])
+    n_heads, rows = cfg.batch * cfg.kv_heads, cfg.group * cfg.query_len
+    need_min = _lib.decode_workspace_min_bytes(n_heads, cfg.seq_len, rows, cfg.head_dim)
+    need_full = int(_lib.load_library().sunshape_decode_workspace_bytes(n_heads, cfg.seq_len, rows, cfg.head_dim,
+                                                                        cfg.n_blocks))
+    assert need_min < need_full
+    ws = torch.zeros(need_min, dtype=torch.uint8, device=DEV)
+    desc, keep, _ = codec.kernel_desc()
+    kd = _lib.kv_desc(qk.indices, qk.heavy, case["value"], cfg.seq_len, cfg.seq_len, cfg.head_dim)
+    ref = _oracle_out(case, qk.indices, qk.heavy, None, case["scale"])
+    for call in range(2):     # the workspace's tickets must be left at zero for the next call
+        out = torch.empty(cfg.batch, cfg.q_heads, 1, cfg.head_dim, device=DEV, dtype=case["value"].dtype)
+        _lib.decode_attention(desc, kd, case["query"], cfg.batch, cfg.q_heads, cfg.kv_heads, 1, None, (0, 0, 0),
+                              case["scale"], out, None, workspace=ws)
+        torch.cuda.synchronize()
+        assert int(ws[:4].view(torch.int32).item()) == 0
+        assert_close_rowwise(out.float().cpu().numpy(), ref, TOL_BF16, f"{name} in-CTA LUT call {call}")
+    # and the LUT-kernel path on the same inputs agrees with it
+    full = vab._apply_quantized_attention(codec=codec, query=case["query"], key=qk, value=case["value"],
+                                          attn_mask=None, scale=case["scale"])
+    assert_close_rowwise(full.float().cpu().numpy(), ref, TOL_BF16, f"{name} LUT kernel")
 
 
 def test_cache_view_head_stride_and_fully_masked_row():
@@ -174,7 +226,7 @@ def test_cache_view_head_stride_and_fully_masked_row():
                                          attn_mask=mask, scale=case["scale"])
     ref = _oracle_out(case, qk.indices, None, mask, case["scale"])
     assert torch.isnan(out[1, 3]).all()
-    assert_close_normwise(out.float().cpu().numpy(), ref, TOL_BF16, "cache view")
+    assert_close_rowwise(out.float().cpu().numpy(), ref, TOL_BF16, "cache view")
 
 
 def test_split_kv_partials_merge_equals_full():
@@ -196,7 +248,7 @@ def test_split_kv_partials_merge_equals_full():
                                          scale=case["scale"]))
     merged = torch.empty(full.numel() // 128, 128, device=DEV, dtype=torch.bfloat16)
     _lib.merge_partials(torch.stack(parts), merged)
-    assert_close_normwise(merged.view_as(full).float().cpu().numpy(), full.float().cpu().numpy(), 1e-2, "merge")
+    assert_close_rowwise(merged.view_as(full).float().cpu().numpy(), full.float().cpu().numpy(), 1e-2, "merge")
 
 
 def test_unsupported_inputs_raise_with_reason():
@@ -214,3 +266,4 @@ def test_no_device_errors_recorded():
 
     torch.cuda.synchronize()
     assert _lib.decode_error_word() == 0
+    assert _lib.encode_error_word(torch.device(DEV)) == 0

@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 from oracle import sunshape_oracle as O
-from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_normwise, load_golden
+from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_rowwise, load_golden
 
 
 def _heads(g, indices, passthrough):
@@ -42,10 +42,10 @@ def test_oracle_scores_match_reference(name):
                 q = O.round_to(q * np.float32(g["scale"]), g["dtype"])
             s = O.attention_scores(q, g["ref_indices"][b, h], g["centroids"][h], g["inv_perm"],
                                    hm if hm.any() else None, g["ref_passthrough"][b, h] if hm.any() else None)
-            assert_close_normwise(s, g["ref_scores"][b, h], TOL_F32, f"{name} scores")
+            assert_close_rowwise(s, g["ref_scores"][b, h], TOL_F32, f"{name} scores")
             s2 = O.lut_scores(q, g["ref_indices"][b, h], g["centroids"][h], g["perm"], hm if hm.any() else None,
                               g["ref_passthrough"][b, h] if hm.any() else None)
-            assert_close_normwise(s2, g["ref_scores"][b, h], TOL_F32, f"{name} lut scores")
+            assert_close_rowwise(s2, g["ref_scores"][b, h], TOL_F32, f"{name} lut scores")
 
 
 @pytest.mark.parametrize("name", GOLDEN_CASES)
@@ -56,7 +56,7 @@ def test_oracle_attention_matches_reference(name):
         centroids_for_head=lambda h: g["centroids"][h], inv_perm=g["inv_perm"], attn_mask=g["mask"],
         scale=g["scale"], query_dtype=g["dtype"], value_dtype=g["dtype"])
     tol = TOL_F32 if g["dtype"] == "f32" else TOL_BF16
-    assert_close_normwise(out, g["ref_out"], tol, f"{name} out")
+    assert_close_rowwise(out, g["ref_out"], tol, f"{name} out")
 
 
 @pytest.mark.parametrize("name", ["g1_c1_fp32", "g2_bf16_mask4d"])

@@ -17,7 +17,7 @@ import torch
 from sunshape_b200 import _lib
 from sunshape_b200 import vllm_attn_backend as vab
 from sunshape_b200.workloads import CONFIGS, make_case
-from tests.helpers import TOL_BF16, assert_close_normwise, make_codec
+from tests.helpers import TOL_BF16, assert_close_rowwise, make_codec
 
 pytestmark = pytest.mark.gpu
 
@@ -37,10 +37,23 @@ def _call_noalloc(codec, keys, query, value, scale):
     return rc, out
 
 
-def test_noalloc_matches_regular_entry_point_twice():
+def _error_word():
+    code = ctypes.c_int32(-1)
+    rc = _lib.load_library().sunshape_decode_attention_noalloc_error(ctypes.byref(code))
+    assert rc == 0, _lib.load_library().sunshape_last_error().decode()
+    return code.value
+
+
+@pytest.mark.parametrize("shape", ["c2_ragged", "c5_headline_heads"])
+def test_noalloc_matches_regular_entry_point_twice(shape):
     dev = torch.device("cuda", 0)
-    # several CTAs share each KV head, so the per-head tickets in the scratch are exercised
-    cfg = CONFIGS["c2"].with_(batch=2, kv_heads=2, q_heads=8, seq_len=20000 + 11)
+    # several CTAs share each KV head, so the per-head tickets in the scratch are exercised;
+    # the second shape has the headline config's 64 KV heads of 8 query rows (fp16 LUT entries),
+    # whose per-head LUT area does not fit the built-in array, so each CTA builds its LUTs
+    if shape == "c2_ragged":
+        cfg = CONFIGS["c2"].with_(batch=2, kv_heads=2, q_heads=8, seq_len=20000 + 11)
+    else:
+        cfg = CONFIGS["c5"].with_(batch=8, kv_heads=8, q_heads=64, seq_len=2048 + 5)
     case = make_case(cfg, device=dev, seed=21)
     codec = make_codec(case["perm"], case["centroids"], case["heavy_mask"], cfg.head_dim, cfg.block_dim,
                        cfg.n_centroids, dev)
@@ -51,7 +64,8 @@ def test_noalloc_matches_regular_entry_point_twice():
         rc, out = _call_noalloc(codec, keys, case["query"], case["value"], case["scale"])
         torch.cuda.synchronize()
         assert rc == 0, _lib.load_library().sunshape_last_error().decode()
-        assert_close_normwise(out.float().cpu().numpy(), ref.float().cpu().numpy(), TOL_BF16, f"noalloc call {call}")
+        assert _error_word() == 0
+        assert_close_rowwise(out.float().cpu().numpy(), ref.float().cpu().numpy(), TOL_BF16, f"noalloc call {call}")
 
 
 def test_noalloc_rejects_workspace_beyond_builtin_scratch():
@@ -72,3 +86,9 @@ def test_noalloc_rejects_workspace_beyond_builtin_scratch():
             _lib.F32, 0, 0, 0, math.nan, value.data_ptr(), _lib.BF16, None, _lib.stream_ptr(dev))
     assert rc == -4
     assert "built-in array" in lib.sunshape_last_error().decode()
+    # an empty batch is accepted without touching the device, as by the regular entry point
+    with torch.cuda.device(dev):
+        rc = lib.sunshape_decode_attention_noalloc(
+            ctypes.byref(desc), ctypes.byref(kd), case["query"].data_ptr(), _lib.BF16, 0, 16, 1, 1, None,
+            _lib.F32, 0, 0, 0, math.nan, value.data_ptr(), _lib.BF16, None, _lib.stream_ptr(dev))
+    assert rc == 0
