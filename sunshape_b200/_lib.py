@@ -217,13 +217,16 @@ _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 def decode_workspace(dev: torch.device, n_heads: int, seq_len: int, rows: int, value_dim: int,
                      n_blocks: int) -> torch.Tensor:
     """Zero-initialised workspace cached per (device, stream); the kernels leave the tickets zeroed."""
-    need = int(load_library().sunshape_decode_workspace_bytes(n_heads, seq_len, rows, value_dim, n_blocks))
+    if os.environ.get("SUNSHAPE_DECODE_LUT") == "cta":     # per-head LUTs built in each CTA (minimum workspace)
+        need = int(load_library().sunshape_decode_workspace_min_bytes(n_heads, seq_len, rows, value_dim))
+    else:
+        need = int(load_library().sunshape_decode_workspace_bytes(n_heads, seq_len, rows, value_dim, n_blocks))
     key = (dev.index if dev.index is not None else torch.cuda.current_device(), stream_ptr(dev))
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < need:
-        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
+        ws = torch.zeros(need, dtype=torch.uint8, device=dev)
         _workspaces[key] = ws
-    return ws
+    return ws[:need]
 
 
 def decode_error_word(dev: torch.device | None = None) -> int:

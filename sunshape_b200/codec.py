@@ -262,12 +262,12 @@ class SunShapeBlockCodec(torch.nn.Module):
         idx = quantized.indices
         if idx.dtype not in (torch.uint8, torch.int16, torch.int32):
             idx = idx.to(torch.int32)
-        idx = idx.contiguous()
+        idx = _lib.aligned16(idx.contiguous())
         heavy = None
         if n_heavy:
             if quantized.passthrough_values is None:
                 raise ValueError("Mixed-precision quantized keys are missing passthrough values.")
-            heavy = quantized.passthrough_values[:, self.heavy_block_ids()].float().contiguous()
+            heavy = _lib.aligned16(quantized.passthrough_values[:, self.heavy_block_ids()].float().contiguous())
         T = idx.shape[0]
         out = torch.empty(T, self.head_dim, device=idx.device, dtype=torch.float32)
         if T:

@@ -26,7 +26,7 @@ __global__ void merge_partials_kernel(const float* __restrict__ parts, int n_par
       for (int k = 0; k < n_parts; ++k) {
         const float* src = parts + (k * rows + r) * (dv + 2);
         if (src[0] == NEG_INF) continue;
-        const float sc = fast_exp2((src[0] - M) * kLog2e);
+        const float sc = expf(src[0] - M);
         Lsum = fmaf(src[1], sc, Lsum);
         A = fmaf(src[2 + d], sc, A);
       }

@@ -45,6 +45,15 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Softmax weight e^d (d <= 0).  The fp32-value path uses the accurate expf so its outputs stay within
+// the fp32 parity bound at large logits; the 16-bit paths use ex2.approx (their P is rounded to
+// 16 bits anyway).
+template <bool PRECISE>
+__device__ __forceinline__ float softmax_weight(float d) {
+  if constexpr (PRECISE) return expf(d);
+  else return fast_exp2(d * kLog2e);
+}
+
 // --------------------------------------------------------------------------
 // mbarrier + bulk copy (cp.async.bulk, the TMA engine's 1-D mode)
 // --------------------------------------------------------------------------

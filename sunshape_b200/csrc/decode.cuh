@@ -361,7 +361,7 @@ __device__ __forceinline__ void signal_peers(const DecodeParams& p, int64_t hh, 
 #else
 #define SUNSHAPE_FMARK(k) ((void)0)
 #endif
-template <int GP, int DV, int NW>
+template <int GP, int DV, int NW, bool PRECISE = false>
 __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t hh, int64_t tb, int64_t grid,
                                int ctid, int* flag_s) {
   constexpr int ROWF = DV + 2;
@@ -381,7 +381,7 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
     if (M != NEG_INF) {
       for (int w = 0; w < NW; ++w) {
         const float* src = stg + (w * GP + r) * ROWF;
-        const float sc = fast_exp2((src[0] - M) * kLog2e);
+        const float sc = softmax_weight<PRECISE>(src[0] - M);
         Lsum = fmaf(src[1], sc, Lsum);
         A = fmaf(src[2 + d], sc, A);
       }
@@ -460,7 +460,7 @@ __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t 
             const float m = staged ? src[0] : __ldcg(src);
             const float l = staged ? src[1] : __ldcg(src + 1);
             const float a = staged ? src[2 + d] : __ldcg(src + 2 + d);
-            const float sc = fast_exp2((m - M) * kLog2e);   // m = -inf (empty slot) -> 0
+            const float sc = softmax_weight<PRECISE>(m - M);   // m = -inf (empty slot) -> 0
             Lsum = fmaf(l, sc, Lsum);
             A = fmaf(a, sc, A);
           }
@@ -644,9 +644,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             if (mnew == NEG_INF) {
               pr[0] = pr[1] = pr[2] = pr[3] = 0.f;
             } else {
-              alpha = fast_exp2((m_run[x] - mnew) * kLog2e);
+              alpha = softmax_weight<sizeof(VT) == 4>(m_run[x] - mnew);
 #pragma unroll
-              for (int qd = 0; qd < 4; ++qd) pr[qd] = fast_exp2((sc[qd][x] - mnew) * kLog2e);
+              for (int qd = 0; qd < 4; ++qd) pr[qd] = softmax_weight<sizeof(VT) == 4>(sc[qd][x] - mnew);
             }
             l_run[x] = l_run[x] * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
             m_run[x] = mnew;
@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
           *reinterpret_cast<float2*>(mine + g * ROWF + 2 + lane * DPL + 2 * k) = acc[g][k];
       named_barrier(kBarConsumers, kConsumerThreads);
 
-      finish_segment<GP, DV, kWarps>(p, stg, hh, tb, grid, ctid, flag_s);
+      finish_segment<GP, DV, kWarps, sizeof(VT) == 4>(p, stg, hh, tb, grid, ctid, flag_s);
     }
     f = fend;
   }

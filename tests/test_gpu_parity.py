@@ -164,8 +164,39 @@ def test_decode_matches_oracle_seeded(name):
     out = vab._apply_quantized_attention(codec=codec, query=case["query"], key=qk, value=case["value"],
                                          attn_mask=mask, scale=scale)
     ref = _oracle_out(case, qk.indices, qk.heavy, mask, scale)
+    if cfg.dtype == "f32" and mask is None:
+        # fp32 at logits of ~80 (no scale): the reference's own fp32 arithmetic is ~1e-5 per row away
+        # from exact arithmetic, so the bound is 1e-5 plus that measured error of the reference
+        exact = _exact_out(case, qk.indices, scale)
+        ref_err = (np.abs(ref - exact).reshape(-1, cfg.head_dim).max(1) /
+                   np.abs(exact).reshape(-1, cfg.head_dim).max(1))
+        ours = out.float().cpu().numpy()
+        err = np.abs(ours - ref).reshape(-1, cfg.head_dim).max(1) / np.abs(ref).reshape(-1, cfg.head_dim).max(1)
+        assert (err <= TOL_F32 + ref_err).all(), (err.max(), ref_err.max())
+        return
     tol = TOL_F32 if cfg.dtype == "f32" else TOL_BF16
     assert_close_rowwise(out.float().cpu().numpy(), ref, tol, name)
+
+
+def _exact_out(case, idx, scale):
+    """fp64 softmax(q k_hat^T) V of an unmasked case (the error-free value of the same quantities)."""
+    cfg = case["cfg"]
+    cents = case["centroids"].cpu().numpy()
+    inv = case["inv_perm"].cpu().numpy()
+    q = case["query"].double().cpu().numpy()
+    v = case["value"].double().cpu().numpy()
+    idx_n = idx.cpu().numpy()
+    G, L = cfg.group, cfg.query_len
+    out = np.zeros((cfg.batch, cfg.q_heads, L, cfg.head_dim))
+    for b in range(cfg.batch):
+        for h in range(cfg.kv_heads):
+            kh = O.dequantize(idx_n[b, h], cents[h], inv).astype(np.float64)
+            qq = q[b, h * G:(h + 1) * G].reshape(-1, cfg.head_dim) * (1.0 if scale is None else scale)
+            s = qq @ kh.T
+            p = np.exp(s - s.max(1, keepdims=True))
+            p /= p.sum(1, keepdims=True)
+            out[b, h * G:(h + 1) * G] = (p @ v[b, h]).reshape(G, L, -1)
+    return out
 
 
 # The in-CTA LUT branch: with the smallest accepted workspace (no room for the per-head LUT area),
