@@ -363,13 +363,14 @@ void run_mma(const DecodePlan& pl, cudaStream_t st) {
 }
 
 int launch_lut(const DecodeParams& p, int gp, bool lut16, int n_heads, cudaStream_t st) {
+  const int ns = num_sms();
   switch (gp * 2 + (lut16 ? 1 : 0)) {
-    case 8: launch_lut_t<4, false>(p, n_heads, st); break;
-    case 9: launch_lut_t<4, true>(p, n_heads, st); break;
-    case 16: launch_lut_t<8, false>(p, n_heads, st); break;
-    case 17: launch_lut_t<8, true>(p, n_heads, st); break;
-    case 32: launch_lut_t<16, false>(p, n_heads, st); break;
-    default: launch_lut_t<16, true>(p, n_heads, st); break;
+    case 8: launch_lut_t<4, false>(p, n_heads, ns, st); break;
+    case 9: launch_lut_t<4, true>(p, n_heads, ns, st); break;
+    case 16: launch_lut_t<8, false>(p, n_heads, ns, st); break;
+    case 17: launch_lut_t<8, true>(p, n_heads, ns, st); break;
+    case 32: launch_lut_t<16, false>(p, n_heads, ns, st); break;
+    default: launch_lut_t<16, true>(p, n_heads, ns, st); break;
   }
   return SUNSHAPE_OK;
 }
@@ -736,9 +737,14 @@ static int decode_impl(const sunshape_codec_t* codec, const sunshape_kv_t* kv, c
     p.slots = reinterpret_cast<float*>(ws + 256 + round_up(n_heads * 4, 256));
     if (use_mma) {
       // per-head LUTs built GPU-wide at kernel start when they fit the workspace policy
-      const int64_t lut_ws = kGlobalLutMaxBytes >= (int64_t)n_heads * p.lut_bytes ? p.lut_bytes : 0;
+      const int64_t lut_ws =
+          (codec->block_dim <= 16 && codec->head_dim % 8 == 0 && aligned16(query) &&
+           kGlobalLutMaxBytes >= (int64_t)n_heads * p.lut_bytes) ? p.lut_bytes : 0;
       const MmaWsOffsets o = mma_workspace_offsets(n_heads, pl.grid, p.max_seg, pl.gp, dv, lut_ws);
       p.slots = reinterpret_cast<float*>(ws + o.slots);
+#ifdef SUNSHAPE_TRACE
+      p.trace = reinterpret_cast<unsigned long long*>(ws + (workspace_bytes - 4096 * 256) / 256 * 256);
+#endif
       if (lut_ws && workspace_bytes >= o.total) {
         p.lut_global = ws + o.luts;
         p.lut_scale_global = reinterpret_cast<float*>(ws + o.scales);

@@ -22,6 +22,8 @@
 //     accumulators, A fragments loaded straight from the swizzled value tile.
 #pragma once
 
+#include <algorithm>
+
 #include "decode.cuh"
 
 namespace sunshape {
@@ -42,6 +44,11 @@ constexpr int kPrefetchAhead = 0;                // tiles prefetched into L2 bey
 // stages, [2] consumer total (sum over warps), [3] consumer waiting on full stages,
 // [4] consumer LUT builds, [5] consumer segment ends, [6] producer issuing copies.
 #ifdef SUNSHAPE_TRACE
+// grid-wide spans of the side kernels: words 148*32 + k of the trace area; even k = earliest start
+// (stored complemented so atomicMax keeps the minimum), odd k = latest end
+#define SUNSHAPE_SPAN_START(k) do { if (threadIdx.x == 0 && p.trace) atomicMax(p.trace + 148 * 32 + (k), ~(unsigned long long)global_ns()); } while (0)
+#define SUNSHAPE_SPAN_END(k) do { if (threadIdx.x == 0 && p.trace) atomicMax(p.trace + 148 * 32 + (k), (unsigned long long)global_ns()); } while (0)
+#define SUNSHAPE_LUTMARK(k) do { if (threadIdx.x == 0 && p.trace) p.trace[148 * 32 + 64 + (blockIdx.y * gridDim.x + blockIdx.x) * 4 + (k)] = global_ns(); } while (0)
 #define SUNSHAPE_TRACE_ADD(slot, v) atomicAdd(reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(p.err) + 64) + (slot), (unsigned long long)(v))
 #define SUNSHAPE_CLK() clock64()
 // per-CTA wall-clock marks (ns) in the trace area at the end of the workspace: [cta][0] start, [1] first tile landed,
@@ -49,6 +56,9 @@ constexpr int kPrefetchAhead = 0;                // tiles prefetched into L2 bey
 #define SUNSHAPE_MARK(k) (p.trace[blockIdx.x * 32 + (k)] = global_ns())
 #else
 #define SUNSHAPE_MARK(k) ((void)0)
+#define SUNSHAPE_SPAN_START(k) ((void)0)
+#define SUNSHAPE_SPAN_END(k) ((void)0)
+#define SUNSHAPE_LUTMARK(k) ((void)0)
 #define SUNSHAPE_TRACE_ADD(slot, v) ((void)0)
 #define SUNSHAPE_CLK() 0ll
 #endif
@@ -268,6 +278,216 @@ __device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s
 }
 
 // Per-head LUTs for one decode launch, in exactly the shared-memory layout the decode kernel
+// uses, written to the workspace.  Organised codebook-major: one CTA per (KV head h, block b, group
+// of hpc sequences) holds codebook block b of h's codebook (thread = codeword, its row in registers)
+// and the query rows of every head (s, h) of the group, and writes the 16-byte LUT entries of all
+// those heads.  A launch is kv_heads x 8*nbh x ceil(batch / hpc) CTAs -- a few hundred -- instead of
+// one CTA per (head, block).  The grid runs while the decode kernel's producers saturate HBM, when
+// every dependent memory round trip costs microseconds, so all global loads (permutation, codebook
+// row, query rows) are issued together in one round; the ProfilePerm gather happens in shared
+// memory.  The decode kernel is launched as a programmatic dependent of this grid: its producer
+// warps start streaming values right away and only its consumers wait (griddepcontrol.wait) before
+// copying their first LUT.
+// Sequences per LUT CTA: enough CTAs to fill the GPU about once (8 per SM), at most 64 and at most
+// 32 KB of query rows in shared memory.
+inline int lut_heads_per_cta(int gp, int D, int items, int batch, int n_sms) {
+  const int cap = std::max(1, std::min(64, 8192 / (gp * D)));
+  const int want = (int)(((int64_t)items * batch) / ((int64_t)n_sms * 8));
+  return std::max(1, std::min(cap, want));
+}
+
+template <int GP, bool L16>
+__global__ void __launch_bounds__(256) lut_cbm_kernel(const __grid_constant__ DecodeParams p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  SUNSHAPE_SPAN_START(0);
+  SUNSHAPE_LUTMARK(0);
+  extern __shared__ float lut_q_s[];                    // [hpc][GP][D] query rows, scaled, unpermuted
+  __shared__ int perm_s[256];
+  __shared__ float scale_s[64];
+  __shared__ unsigned qn_s[64];
+  __shared__ float cn_s;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int D = p.D, bd = p.bd;
+  const int batch = p.n_heads / p.kv_heads;
+  const int hpc = (batch + gridDim.y - 1) / gridDim.y;   // sequences per CTA, set by the launch
+  const int kvh = blockIdx.x / (p.nbh * 8);
+  const int b = blockIdx.x - kvh * (p.nbh * 8);    // block (padding blocks >= nb get zero entries)
+  const int s0 = blockIdx.y * hpc;
+  const int nh = min(hpc, batch - s0);
+  const bool active = b < p.nb && (p.heavy_mask == nullptr || p.heavy_mask[b] == 0);
+  const int cbh = p.n_cb == 1 ? 0 : kvh % p.n_cb;
+  // ---- one round of independent global loads: permutation, this thread's codeword row, query rows
+  for (int i = tid; i < D; i += 256) perm_s[i] = (int)__ldg(p.perm + i);
+  if (tid < 64) qn_s[tid] = 0u;
+  float cw[16];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) cw[d] = 0.f;
+  const int c = tid;
+  if (active && c < p.C) {
+    const float* cr = p.cb + (((int64_t)cbh * p.nb + b) * p.C + c) * bd;
+    if (bd == 8) {
+      const float4 v0 = __ldg(reinterpret_cast<const float4*>(cr)), v1 = __ldg(reinterpret_cast<const float4*>(cr) + 1);
+      cw[0] = v0.x; cw[1] = v0.y; cw[2] = v0.z; cw[3] = v0.w; cw[4] = v1.x; cw[5] = v1.y; cw[6] = v1.z; cw[7] = v1.w;
+    } else if (bd == 4) {
+      const float4 v0 = __ldg(reinterpret_cast<const float4*>(cr));
+      cw[0] = v0.x; cw[1] = v0.y; cw[2] = v0.z; cw[3] = v0.w;
+    } else {
+      for (int d = 0; d < bd; ++d) cw[d] = __ldg(cr + d);
+    }
+  }
+  {
+    // query rows of the group: 16-byte vector loads, all issued before the first use (one round trip)
+    const int rowv = D / 8;                        // 8-element chunks per row
+    const int totv = hpc * GP * rowv;
+    const int es = p.q_dtype == SUNSHAPE_F32 ? 4 : 2;
+    constexpr int kMaxV = 8;                       // chunks per thread: hpc * GP * D <= 8192 elements
+    uint4 raw[kMaxV][2];
+#pragma unroll
+    for (int u = 0; u < kMaxV; ++u) {
+      const int e = tid + u * 256;
+      const int j = e / (GP * rowv), r = e - j * GP * rowv, g = r / rowv, ch = r - g * rowv;
+      raw[u][0] = raw[u][1] = make_uint4(0u, 0u, 0u, 0u);
+      if (e < totv && j < nh && g < p.Rc) {
+        const int64_t hh = (int64_t)(s0 + j) * p.kv_heads + kvh;
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.q) +
+                                                          ((hh * p.R + p.r0 + g) * D + ch * 8) * es);
+        raw[u][0] = __ldg(src);
+        if (es == 4) raw[u][1] = __ldg(src + 1);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kMaxV; ++u) {
+      const int e = tid + u * 256;
+      if (e >= totv) break;
+      float x[8];
+      if (es == 4) {
+        const uint32_t w[8] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w,
+                               raw[u][1].x, raw[u][1].y, raw[u][1].z, raw[u][1].w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = __uint_as_float(w[i]);
+      } else {
+        const uint32_t w[4] = {raw[u][0].x, raw[u][0].y, raw[u][0].z, raw[u][0].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (p.q_dtype == SUNSHAPE_BF16) {
+            x[2 * i] = __uint_as_float(w[i] << 16);
+            x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+          } else {
+            x[2 * i] = __half2float(__ushort_as_half((unsigned short)(w[i] & 0xffffu)));
+            x[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)(w[i] >> 16)));
+          }
+        }
+      }
+      if (p.has_scale) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = round_to_dtype(x[i] * p.scale, p.q_dtype);
+      }
+      float4* dst = reinterpret_cast<float4*>(lut_q_s + (int64_t)e * 8);
+      dst[0] = make_float4(x[0], x[1], x[2], x[3]);
+      dst[1] = make_float4(x[4], x[5], x[6], x[7]);
+    }
+  }
+  if (L16 && p.cb_norm_max == nullptr) {   // fallback bound (C ABI callers without norms): bd * max c_i^2
+    float cn = 0.f;
+    const float* cbf = p.cb + (int64_t)cbh * p.nb * p.C * bd;
+    for (int e = tid; e < p.nb * p.C * bd; e += 256) cn = fmaxf(cn, cbf[e] * cbf[e] * bd);
+    cn = warp_max(cn);
+    if (tid == 0) cn_s = 0.f;
+    __syncthreads();
+    if (lane == 0) atomicMax(reinterpret_cast<int*>(&cn_s), __float_as_int(cn));
+  }
+  __syncthreads();
+  SUNSHAPE_LUTMARK(1);
+  if constexpr (L16) {
+    // fp16 entries are scaled by a power of two from the bound |q_b . c| <= max_b |q_b| * max |c|
+    // (max over the head's rows and blocks), so no entry can overflow: one thread per (head, row, block)
+    for (int e = tid; e < nh * GP * p.nb; e += 256) {
+      const int j = e / (GP * p.nb), r = e - j * GP * p.nb, g = r / p.nb, bb = r - g * p.nb;
+      const float* qr = lut_q_s + ((int64_t)j * GP + g) * D;
+      float a = 0.f;
+      for (int d = 0; d < bd; ++d) {
+        const float x = qr[perm_s[bb * bd + d]];
+        a = fmaf(x, x, a);
+      }
+      atomicMax(&qn_s[j], __float_as_uint(a));   // non-negative floats order like their bits
+    }
+    __syncthreads();
+    if (tid < nh) {
+      const int j = tid;
+      float cn;
+      if (p.cb_norm_max != nullptr) {
+        const float m = __ldg(p.cb_norm_max + cbh);
+        cn = m * m;
+      } else {
+        cn = cn_s;
+      }
+      const float bound = sqrtf(__uint_as_float(qn_s[j])) * sqrtf(cn) * 1.001f;
+      const float scale = bound > 0.f ? exp2f(fminf(100.f, floorf(log2f(32768.f / bound)))) : 1.f;
+      scale_s[j] = scale;
+      if (b == 0) p.lut_scale_global[(int64_t)(s0 + j) * p.kv_heads + kvh] = 1.f / scale;
+    }
+    __syncthreads();
+  } else {
+    if (b == 0 && tid < nh) p.lut_scale_global[(int64_t)(s0 + tid) * p.kv_heads + kvh] = 1.f;
+  }
+  SUNSHAPE_LUTMARK(2);
+  if (c >= p.C) return;
+  const int kh = b >> 3, blo = b & 7;
+  constexpr int NH = L16 ? (GP >= 8 ? GP / 8 : 1) : GP / 4;
+  int pb[16];
+#pragma unroll
+  for (int d = 0; d < 16; ++d) pb[d] = (active && d < bd) ? perm_s[b * bd + d] : 0;
+  for (int j = 0; j < nh; ++j) {
+    float v[GP];
+#pragma unroll
+    for (int g = 0; g < GP; ++g) {
+      const float* qr = lut_q_s + ((int64_t)j * GP + g) * D;
+      float a = 0.f;
+      if (bd == 8) {
+#pragma unroll
+        for (int d = 0; d < 8; ++d) a = fmaf(qr[pb[d]], cw[d], a);
+      } else if (bd == 4) {
+#pragma unroll
+        for (int d = 0; d < 4; ++d) a = fmaf(qr[pb[d]], cw[d], a);
+      } else {
+#pragma unroll
+        for (int d = 0; d < 16; ++d)
+          if (d < bd) a = fmaf(qr[pb[d]], cw[d], a);
+      }
+      v[g] = a;
+    }
+    const int64_t hh = (int64_t)(s0 + j) * p.kv_heads + kvh;
+    uint8_t* base = p.lut_global + hh * (int64_t)p.lut_bytes;
+    uint8_t* dst = (L16 && GP == 4) ? base + (int64_t)(kh >> 1) * kLutC * 128 + blo * 16 + (kh & 1) * 8
+                                    : base + (int64_t)kh * NH * kLutC * 128 + blo * 16;
+    store_lut_entry<GP, L16>(dst, c, v, L16 ? scale_s[j] : 1.f);
+  }
+  SUNSHAPE_SPAN_END(1);
+  SUNSHAPE_LUTMARK(3);
+}
+
+template <int GP, bool L16>
+void launch_lut_head_block_t(const DecodeParams& prm, int n_heads, cudaStream_t st);
+// LUT build strategy: one CTA per (head, block) while that grid fits the GPU in a few waves; beyond
+// that (many heads) the codebook-major grid, which loads each codebook block once per group of
+// sequences.  (Measured on B200: head/block is faster at 64-128 heads x 16 blocks, codebook-major
+// at 512 heads x 16 blocks.)
+template <int GP, bool L16>
+void launch_lut_t(const DecodeParams& prm, int n_heads, int n_sms, cudaStream_t st) {
+  if ((int64_t)n_heads * prm.nbh * 8 <= (int64_t)n_sms * 32) {
+    launch_lut_head_block_t<GP, L16>(prm, n_heads, st);
+    return;
+  }
+  const int batch = n_heads / prm.kv_heads;
+  const int items = prm.kv_heads * prm.nbh * 8;
+  const int hpc = lut_heads_per_cta(GP, prm.D, items, batch, n_sms);
+  const int groups = (batch + hpc - 1) / hpc;
+  const int hpc_eff = (batch + groups - 1) / groups;   // what the kernel derives from gridDim.y
+  const size_t smem = (size_t)hpc_eff * GP * prm.D * sizeof(float);
+  lut_cbm_kernel<GP, L16><<<dim3(items, groups), 256, smem, st>>>(prm);
+}
+
+// Per-head LUTs for one decode launch, in exactly the shared-memory layout the decode kernel
 // uses, written to the workspace: one CTA per (KV head, block), one thread per codeword, so the
 // whole GPU builds all LUTs in a couple of memory round trips.  The decode kernel is launched as
 // a programmatic dependent of this grid: its producer warps start streaming values right away and
@@ -356,7 +576,7 @@ __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ Decode
 }
 
 template <int GP, bool L16>
-void launch_lut_t(const DecodeParams& prm, int n_heads, cudaStream_t st) {
+void launch_lut_head_block_t(const DecodeParams& prm, int n_heads, cudaStream_t st) {
   lut_kernel<GP, L16><<<dim3(n_heads, prm.nbh * 8), 256, 0, st>>>(prm);
 }
 
@@ -857,23 +1077,23 @@ template <int GP, int DV, typename VT, bool L16>
 void launch_decode_mma_t(const DecodeLaunch& l, cudaStream_t st) {
   auto k = decode_mma_kernel<GP, DV, VT, L16>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, l.smem);
-  if (l.prm.lut_global == nullptr) {
-    k<<<(unsigned)l.grid, kThreadsM, l.smem, st>>>(l.prm);
-    return;
-  }
-  // programmatic dependent launch after lut_kernel: this grid may start while the LUTs are being
-  // built; its consumers wait for them with griddepcontrol.wait
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)l.grid);
-  cfg.blockDim = dim3(kThreadsM);
-  cfg.dynamicSmemBytes = (size_t)l.smem;
-  cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k, l.prm);
+  if (l.prm.lut_global == nullptr) {
+    k<<<(unsigned)l.grid, kThreadsM, l.smem, st>>>(l.prm);
+  } else {
+    // programmatic dependent launch after lut_kernel: this grid may start while the LUTs are being
+    // built; its consumers wait for them with griddepcontrol.wait
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)l.grid);
+    cfg.blockDim = dim3(kThreadsM);
+    cfg.dynamicSmemBytes = (size_t)l.smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, k, l.prm);
+  }
 }
 
 
