@@ -490,13 +490,14 @@ int sunshape_encode(const sunshape_codec_t* codec, const void* keys, int32_t key
   // SUNSHAPE_ENCODE=cuda_cores forces the CUDA-core kernel (a cross-check of the tensor-core one)
   const char* path = getenv("SUNSHAPE_ENCODE");
   const bool force_cc = path && strcmp(path, "cuda_cores") == 0;
-  if (!force_cc && encode_tc_supported(p)) {
-    launch_encode_tc(p, n_heads, st);
+  if (!force_cc && encode_tc_supported(p) &&
+      launch_encode_tc(p, n_heads, codec->heavy_mask ? codec->n_heavy : 0, st) == 0)
     return cuda_status("encode (tensor cores) launch");
-  }
   if (path && strcmp(path, "tensor_cores") == 0)
-    return fail(SUNSHAPE_E_UNSUPPORTED, "SUNSHAPE_ENCODE=tensor_cores: needs bf16/f16 keys with 16-byte aligned rows, "
-                                        "block_dim 2, 4 or 8 and n_centroids a multiple of 16 up to 256.");
+    return fail(SUNSHAPE_E_UNSUPPORTED, "SUNSHAPE_ENCODE=tensor_cores: needs fp32/bf16/f16 keys with 16-byte multiple "
+                                        "row and head strides, head_dim * element size a multiple of 128 bytes, "
+                                        "block_dim 2, 4 or 8, at most 64 blocks and n_centroids a multiple of 64 up "
+                                        "to 256.");
   const int smem = (kEncRows * (D + 1) + C * bd + C + D) * 4 + 64;
   if (smem > kSmemLimit) return fail(SUNSHAPE_E_UNSUPPORTED, "encode: codebook too large for shared memory.");
   dim3 grid((n_tokens + kEncRows - 1) / kEncRows, n_heads);

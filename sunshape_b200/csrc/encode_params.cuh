@@ -28,7 +28,8 @@ struct EncodeParams {
 
 // tensor-core (tcgen05) encode, encode_tc.cu
 bool encode_tc_supported(const EncodeParams& p);
-int launch_encode_tc(const EncodeParams& p, int n_heads, cudaStream_t st);
+// returns 0 when launched, -1 when this shape must use encode_kernel instead
+int launch_encode_tc(const EncodeParams& p, int n_heads, int n_heavy, cudaStream_t st);
 // read (and optionally clear) the encode kernels' device error word; returns a cudaError_t
 int encode_error_word(int* code, bool clear);
 

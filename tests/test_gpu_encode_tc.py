@@ -1,6 +1,7 @@
 """Tensor-core (tcgen05) key encode: parity with the reference's indices and with the CUDA-core kernel.
 
-16-bit keys with block_dim 2, 4 or 8 and n_centroids a multiple of 16 (<= 256) take the tensor-core kernel;
+fp32 and 16-bit keys with block_dim 2, 4 or 8 and n_centroids a multiple of 64 (<= 256) take the
+tensor-core kernel;
 ``SUNSHAPE_ENCODE=cuda_cores`` forces the CUDA-core kernel and ``SUNSHAPE_ENCODE=tensor_cores``
 makes an unsupported shape an error, so these tests know which kernel ran.  Indices must agree
 exactly except where two codewords are at the same distance within fp32 rounding (the rule of
@@ -67,17 +68,22 @@ def test_tensor_core_encode_matches_oracle_on_golden_keys(name):
     _check_ties(kb, g["perm"], g["centroids"], hm, qk.indices.cpu().numpy(), ref, name)
 
 
-@pytest.mark.parametrize("cfg_name,dtype,seq_len,n_centroids", [
-    ("c2", torch.bfloat16, 1000 + 37, 256),     # ragged tail tile
-    ("c3", torch.bfloat16, 4096, 256),          # block_dim 4
-    ("c4", torch.bfloat16, 777, 256),           # SunShape-Mixed heavy blocks
-    ("c5", torch.float16, 300, 64),             # f16 keys, 64 codewords (3 CTAs per SM)
-    ("c2", torch.bfloat16, 1, 16),              # one key, 16 codewords
-    ("c2b2", torch.bfloat16, 515, 64),          # block_dim 2
+@pytest.mark.parametrize("cfg_name,dtype,seq_len,n_centroids,batch", [
+    ("c2", torch.bfloat16, 1000 + 37, 256, 1),    # ragged tail tile
+    ("c3", torch.bfloat16, 4096, 256, 1),         # block_dim 4
+    ("c4", torch.bfloat16, 777, 256, 1),          # SunShape-Mixed heavy blocks
+    ("c5", torch.float16, 300, 64, 1),            # f16 keys, 64 codewords
+    ("c2", torch.bfloat16, 1, 64, 1),             # one key
+    ("c2b2", torch.bfloat16, 515, 64, 1),         # block_dim 2
+    ("c2", torch.float32, 1000 + 37, 256, 1),     # fp32 keys (3xTF32), ragged tail
+    ("c3", torch.float32, 3000, 256, 2),          # fp32, block_dim 4, 16 heads of per-KV-head codebooks
+    ("c4", torch.float32, 700, 256, 1),           # fp32 SunShape-Mixed
+    ("c2b2", torch.float32, 333, 128, 1),         # fp32, block_dim 2, 128 codewords
+    ("c5", torch.float32, 2, 256, 1),             # fp32, two keys per head
 ])
-def test_tensor_core_encode_matches_cuda_core_kernel(cfg_name, dtype, seq_len, n_centroids):
+def test_tensor_core_encode_matches_cuda_core_kernel(cfg_name, dtype, seq_len, n_centroids, batch):
     base = CONFIGS[cfg_name[:2]].with_(block_dim=2) if cfg_name == "c2b2" else CONFIGS[cfg_name]
-    cfg = base.with_(batch=1, seq_len=seq_len, n_centroids=n_centroids)
+    cfg = base.with_(batch=batch, seq_len=seq_len, n_centroids=n_centroids)
     case = make_case(cfg, device=DEV, seed=5)
     codec = make_codec(case["perm"], case["centroids"], case["heavy_mask"], cfg.head_dim, cfg.block_dim,
                        cfg.n_centroids, DEV)
@@ -96,10 +102,12 @@ def test_tensor_core_encode_matches_cuda_core_kernel(cfg_name, dtype, seq_len, n
     assert agree > 0.999, f"only {agree:.5f} of indices agree"
     if tc.heavy is not None:
         assert torch.equal(tc.heavy, cc.heavy)
+    from sunshape_b200 import _lib
+    assert _lib.encode_error_word(torch.device(DEV)) == 0
 
 
-def test_tensor_core_encode_rejects_fp32_keys_when_forced():
-    cfg = CONFIGS["c2"].with_(batch=1, seq_len=64)
+def test_tensor_core_encode_rejects_unsupported_shape_when_forced():
+    cfg = CONFIGS["c2"].with_(batch=1, seq_len=64, n_centroids=48)
     case = make_case(cfg, device=DEV, seed=1)
     codec = make_codec(case["perm"], case["centroids"], case["heavy_mask"], cfg.head_dim, cfg.block_dim,
                        cfg.n_centroids, DEV)
