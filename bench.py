@@ -441,11 +441,13 @@ def run_ours(args, cfg: DecodeConfig):
     barrier()
     clocks = sampler.stop()
 
+    parity = None
     if world > 1:
         import torch.distributed as dist
         t = torch.tensor([t_ms, e2e_ms, kernel_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         t_ms, e2e_ms, kernel_ms = t.tolist()
+        parity = multi_gpu_parity(args, rank, world, dev)
 
     total_tokens = cfg.kv_tokens()
     ms_per_step = t_ms / args.steps
@@ -480,9 +482,52 @@ def run_ours(args, cfg: DecodeConfig):
                 "d2h_bytes_per_step": out.numel() * out.element_size()},
         "clocks": clocks,
         "gpu_launches": args.steps * launches_per_step,
+        **({"decode_ms": kernel_ms, "exchange_ms": max(0.0, ms_per_step - kernel_ms), "parity": parity}
+           if world > 1 else {}),
         "timing": "device-side: CUDA-graph replay of whole steps (all launches of every step); e2e: eager public-API calls",
     }
     return res, rank, world
+
+
+def multi_gpu_parity(args, rank: int, world: int, dev: torch.device) -> dict:
+    """Before trusting the scaling numbers: a seeded c5-shaped case (2 sequences, 16/2 heads, ragged
+    4099-token context) decoded through KVShardedDecode with this run's exchange, three calls with
+    different queries, against the single-GPU fused decode of the unsharded cache on the same rank
+    (the path the -m gpu tests check against the reference).  Worst per-row relative error, max over
+    ranks; ok = within the bf16 output tolerance 2e-2."""
+    import torch.distributed as dist
+    from sunshape_b200 import vllm_attn_backend as vab
+    from sunshape_b200.codec import SunShapeBlockCodec
+    from sunshape_b200.distributed import KVShardedDecode, kv_shard_bounds
+
+    cfg = CONFIGS["c5"].with_(batch=2, kv_heads=2, q_heads=16, seq_len=4099)
+    case = make_case(cfg, device=dev, seed=17)
+    codec = SunShapeBlockCodec(cfg.head_dim, cfg.block_dim, cfg.n_centroids, device=dev, kv_heads=cfg.kv_heads)
+    codec.permutation.copy_(case["perm"])
+    codec.inv_permutation.copy_(case["inv_perm"])
+    codec.centroids.copy_(case["centroids"])
+    codec.invalidate()
+    qk = vab.quantize_codec_keys(codec, case["keys"])
+    a, b = kv_shard_bounds(cfg.seq_len, world, rank)
+    shard = vab.SunShapeQuantizedKeys((), cfg.batch, cfg.kv_heads, b - a, indices=qk.indices[:, :, a:b].contiguous())
+    v = case["value"][:, :, a:b].contiguous()
+    dec = KVShardedDecode(codec, exchange=args.exchange)
+    worst = 0.0
+    for call in range(3):
+        q = case["query"] * (1.0 + 0.25 * call)
+        ref = vab._apply_quantized_attention(codec=codec, query=q, key=qk, value=case["value"], attn_mask=None,
+                                             scale=case["scale"]).float()
+        out = dec(q, shard, v, scale=case["scale"]).float()
+        err = ((out - ref).abs().amax(-1) / ref.abs().amax(-1).clamp_min(1e-30)).max().item()
+        worst = max(worst, err if err == err else float("inf"))
+    torch.cuda.synchronize()
+    dist.barrier()
+    dec.close()
+    t = torch.tensor([worst], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    worst = float(t.item())
+    return {"max_rel_err_per_row": worst, "ok": worst <= 2e-2, "calls": 3,
+            "against": "single-GPU fused decode of the unsharded cache", "case": "c5-shaped B2 16/2 heads T4099"}
 
 
 def run_extra_configs(args):
@@ -575,8 +620,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--seq-len", type=int, default=0,
                     help="override the workload's context length (small cases for profiler captures)")
-    ap.add_argument("--exchange", choices=["nccl", "peer"], default="nccl",
-                    help="N>1 merge: NCCL all-gather + merge kernel, or peer-memory stores from the decode kernel")
+    ap.add_argument("--exchange", choices=["nccl", "peer", "p2p"], default="nccl",
+                    help="N>1 merge: NCCL all-gather + merge kernel; peer-memory stores from the decode kernel; or "
+                         "one exchange kernel pushing partials over NVLink and merging (p2p)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.workload]

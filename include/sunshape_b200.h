@@ -176,6 +176,21 @@ int sunshape_decode_attention_peers(const sunshape_codec_t* codec, const sunshap
                                     const sunshape_peer_group_t* group,
                                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ---- Cross-GPU merge of per-rank partials over NVLink peer memory (no reference counterpart).
+ * Each rank allocates one buffer of sunshape_exchange_buffer_bytes(world, rows, value_dim) with
+ * sunshape_peer_alloc and maps every other rank's with sunshape_peer_open.  sunshape_exchange_merge
+ * takes this rank's partials [rows, 2 + value_dim] fp32 (as written by sunshape_decode_attention),
+ * pushes them into every rank's buffer with 16-byte peer stores, waits (bounded, 2 s) for every
+ * rank's rows and writes the merged output out [rows, value_dim] of out_dtype -- one kernel, no
+ * library collective.  All ranks must make the same sequence of calls; the call count lives in the
+ * buffers.  sunshape_exchange_error reads this rank's buffer error word (105 = a wait gave up; that
+ * call's output rows are NaN). */
+int64_t sunshape_exchange_buffer_bytes(int32_t world, int64_t rows, int32_t value_dim);
+int sunshape_exchange_merge(const float* partials, int64_t rows, int32_t value_dim,
+                            const sunshape_peer_group_t* group, void* out, int32_t out_dtype, void* stream);
+int sunshape_exchange_error(const void* own_buffer, int32_t world, int64_t rows, int32_t value_dim,
+                            int32_t* code);
+
 /* Size of the scratch array built into the library for sunshape_decode_attention_noalloc. */
 #define SUNSHAPE_NOALLOC_SCRATCH_BYTES (8 * 1024 * 1024)
 

@@ -30,7 +30,8 @@ EXPORTED_SYMBOLS = (
     "sunshape_merge_partials", "sunshape_decode_attention_noalloc", "sunshape_peer_buffer_bytes",
     "sunshape_peer_alloc", "sunshape_peer_open", "sunshape_peer_close", "sunshape_peer_free",
     "sunshape_decode_attention_peers", "sunshape_decode_workspace_min_bytes", "sunshape_encode_error",
-    "sunshape_decode_attention_noalloc_error",
+    "sunshape_decode_attention_noalloc_error", "sunshape_exchange_buffer_bytes", "sunshape_exchange_merge",
+    "sunshape_exchange_error",
 )
 
 
@@ -98,6 +99,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sunshape_encode_error.restype = ctypes.c_int
         lib.sunshape_decode_attention_noalloc_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
         lib.sunshape_decode_attention_noalloc_error.restype = ctypes.c_int
+        lib.sunshape_exchange_buffer_bytes.argtypes = [i32, i64, i32]
+        lib.sunshape_exchange_buffer_bytes.restype = ctypes.c_int64
+        lib.sunshape_exchange_merge.argtypes = [vp, i64, i32, ctypes.POINTER(PeerGroupDesc), vp, i32, vp]
+        lib.sunshape_exchange_merge.restype = ctypes.c_int
+        lib.sunshape_exchange_error.argtypes = [vp, i32, i64, i32, ctypes.POINTER(ctypes.c_int32)]
+        lib.sunshape_exchange_error.restype = ctypes.c_int
         lib.sunshape_merge_partials.argtypes = [vp, i32, i64, i32, vp, i32, vp]
         lib.sunshape_decode_attention_noalloc.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64,
                                                           i64, f32, vp, i32, vp, vp]
@@ -288,3 +295,12 @@ def decode_attention_peers(cd: CodecDesc, kd: KVDesc, query: torch.Tensor, batch
             ptr(mask), dtype_code(mask) if mask is not None else F32, *mask_strides,
             math.nan if scale is None else float(scale), ptr(out), dtype_code(out), ctypes.byref(group), ptr(ws),
             ws.numel(), stream_ptr(dev)))
+
+
+def exchange_merge(parts: torch.Tensor, out: torch.Tensor, group: PeerGroupDesc) -> None:
+    """parts [rows, 2 + Dv] fp32 (this rank's) -> out [rows, Dv] merged over every rank of ``group``."""
+    dev = require_cuda(parts, out)
+    with torch.cuda.device(dev):
+        _check(load_library().sunshape_exchange_merge(ptr(parts), int(parts.shape[0]), int(parts.shape[1] - 2),
+                                                      ctypes.byref(group), ptr(out), dtype_code(out),
+                                                      stream_ptr(dev)))

@@ -98,6 +98,9 @@ class KVShardedDecode:
     """Decode attention over a KV cache whose sequence is split across the ranks of ``group``.
 
     ``exchange="nccl"`` (default): partials, one NCCL all-gather, merge kernel.
+    ``exchange="p2p"`` (CUDA, at most 8 ranks): partials, then ONE exchange kernel per rank that pushes
+    them into every rank's exchange buffer over NVLink (16-byte peer stores, per-slice flags) and merges
+    all ranks' rows as soon as they land (``sunshape_exchange_merge``); no library collective.
     ``exchange="peer"`` (CUDA, 16-bit values, at most 8 ranks): ranks write their per-head results
     straight into every peer's exchange buffer from inside the decode kernel (CUDA IPC mappings,
     NVLink stores, system-scope arrival counters), then one merge kernel per rank combines them; no
@@ -121,6 +124,19 @@ class KVShardedDecode:
         return decode_partials(codec=self.codec, query=query, key=key, value=value, attn_mask=attn_mask,
                                scale=scale, partials=self._partials)
 
+    def _p2p_group(self, query, value) -> "PeerGroup | None":
+        if self.exchange != "p2p" or not query.is_cuda or dist.get_world_size(self.group) > 8:
+            return None
+        B, Hq, L, _ = query.shape
+        Dv = value.shape[-1]
+        key = ("p2p", B * Hq * L, Dv, query.device)
+        pg = self._peers.get(key)
+        if pg is None:
+            nbytes = _lib.load_library().sunshape_exchange_buffer_bytes(dist.get_world_size(self.group),
+                                                                        B * Hq * L, Dv)
+            pg = self._peers[key] = PeerGroup(nbytes, query.device, self.group)
+        return pg
+
     def _peer_group(self, query, value) -> "PeerGroup | None":
         if self.exchange != "peer" or not query.is_cuda or value.dtype == torch.float32:
             return None
@@ -143,8 +159,13 @@ class KVShardedDecode:
             return _apply_quantized_attention(codec=self.codec, query=query, key=key, value=value,
                                               attn_mask=attn_mask, scale=scale, peer_group=pg.desc)
         part = self.partials(query, key, value, attn_mask, scale)
-        gathered = gather_partials(part, self.group)
         B, Hq, L, _ = query.shape
+        x = self._p2p_group(query, value)
+        if x is not None:
+            out = torch.empty(B, Hq, L, value.shape[-1], device=query.device, dtype=value.dtype)
+            _lib.exchange_merge(part, out.view(B * Hq * L, -1), x.desc)
+            return out
+        gathered = gather_partials(part, self.group)
         return merge_gathered(gathered, (B, Hq, L, value.shape[-1]), value.dtype)
 
     __call__ = forward

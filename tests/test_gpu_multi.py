@@ -42,7 +42,7 @@ def _worker(rank, world, port, q):
                                           indices=qk.indices[:, :, a:b].contiguous())
         v = case["value"][:, :, a:b].contiguous()
         errs = {}
-        for mode in ("peer", "nccl"):
+        for mode in ("p2p", "peer", "nccl"):
             dec = KVShardedDecode(codec, exchange=mode)
             worst = 0.0
             for call in range(3):
