@@ -256,8 +256,8 @@ int64_t mma_workspace_bytes(int64_t n_heads, int64_t grid, int64_t max_seg, int6
 bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd, int hsize, int n_heads, int T,
                      int rows, std::string& why) {
   const int nbh = (nb + 7) / 8;
-  if (nbh > 4) {
-    why = "n_blocks > 32 is not supported by the fused LUT kernel (LUT would not fit in shared memory).";
+  if (nbh > 8) {
+    why = "n_blocks > 64 is not supported by the fused LUT kernel (LUT would not fit in shared memory).";
     return false;
   }
   if (dv != 64 && dv != 128 && dv != 256) {
@@ -275,7 +275,7 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
     const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
     const int off_perm = 256;
     const int off_hslot = off_perm + round_up(D * 4, 16);
-    const int off_q = round_up(off_hslot + 64, 16);
+    const int off_q = round_up(off_hslot + 128, 16);
     const int off_p = round_up(off_q + gp * D * 4, 16);
     const int off_lut = round_up(off_p + kWarpsM * (nt * 512 + 64), 128);
     const int off_stage = round_up(off_lut + region, 1024);

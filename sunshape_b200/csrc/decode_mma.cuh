@@ -700,7 +700,7 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
   uint64_t* lut_bar = reinterpret_cast<uint64_t*>(smem + 232);   // LUT bulk copy completion
   int* perm_s = reinterpret_cast<int*>(smem + p.off_perm);
   int8_t* hslot_s = reinterpret_cast<int8_t*>(smem + p.off_hslot);
-  int8_t* hlist_s = hslot_s + 32;                 // heavy block ids in slot order
+  int8_t* hlist_s = hslot_s + 64;                 // heavy block ids in slot order
   float* q_s = reinterpret_cast<float*>(smem + p.off_q);
   uint8_t* pbuf = smem + p.off_p;
   uint8_t* lut = smem + p.off_lut;
@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
           // opposite order, so the two 8-byte halves of a slot are read by different lanes
           const int kswap = (L16 && GP == 4) ? ((lane >> 3) & 1) : 0;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
+          for (int kk = 0; kk < 8; ++kk) {   // block groups of 8 (up to 64 blocks)
             if (kk >= p.nbh) break;
             const int kh = kk ^ kswap;
             uint64_t w;

@@ -74,6 +74,11 @@ def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, 
     h = codec._require_head(kv_head, "sunshape_attention_scores")
     if h is not None:
         codec = codec._head_view(h)
+    if codec.n_blocks > 32:
+        # more than 32 blocks (block_dim 2, the reference's default 4 bits/dim): a per-query LUT would
+        # outgrow shared memory, so scores are the reference's own formula (triton_kernels.py:300-311)
+        # on the GPU: the dequantize kernel, then one cuBLAS matmul
+        return _torch_attention_scores(codec, query, quantized_key)
     desc, keep, n_heavy = codec.kernel_desc()
     idx = quantized_key.indices
     if idx.dtype != torch.uint8:

@@ -331,6 +331,9 @@ def _apply_quantized_attention(*, codec, query: torch.Tensor, key: SunShapeQuant
         raise RuntimeError("quantized attention over an empty KV sequence.")
     if n_heavy and heavy is None:
         raise ValueError("Mixed-precision quantized keys are missing passthrough values.")
+    if codec.n_blocks > 32 and value.dtype == torch.float32 and peer_group is None:
+        return _apply_dequantized_attention(codec=codec, query=query, key=key, value=value, attn_mask=attn_mask,
+                                            scale=scale, partials=partials, out=out, write_output=write_output)
     v, idx, heavy, hs = _kv_layout(value, idx, heavy, B, Hkv, T)
     if idx.dtype != torch.uint8:
         idx = idx.to(torch.uint8)
@@ -347,6 +350,41 @@ def _apply_quantized_attention(*, codec, query: torch.Tensor, key: SunShapeQuant
         _lib.decode_attention_peers(desc, kd, q, B, Hq, Hkv, L, mask, mstr, scale, out, peer_group)
     else:
         _lib.decode_attention(desc, kd, q, B, Hq, Hkv, L, mask, mstr, scale, out, partials)
+    return out
+
+
+def _apply_dequantized_attention(*, codec, query, key, value, attn_mask, scale, partials=None, out=None,
+                                 write_output=True):
+    """fp32 values with more than 32 blocks per head (the fused fp32-value kernel keeps its LUT in
+    shared memory): the reference's arithmetic (vllm_attn_backend.py:216-253) on the GPU -- keys from
+    the dequantize kernel, then batched matmul / softmax / matmul in fp32."""
+    B, Hq, L, D = query.shape
+    _, Hkv, T, Dv = value.shape
+    G = Hq // Hkv
+    k_hat = dequantize_keys(codec, key)                                  # [B, Hkv, T, D] fp32
+    q = query if scale is None else query * float(scale)
+    q = q.float().reshape(B, Hkv, G * L, D)
+    s = torch.matmul(q, k_hat.transpose(-2, -1))                          # [B, Hkv, G*L, T]
+    if attn_mask is not None:
+        m = attn_mask.to(device=s.device, dtype=s.dtype)
+        if m.ndim == 3:   # [batch, L, T] or [q_heads, L, T] (vllm_attn_backend.py:197-213 order)
+            m = m[:, None] if m.shape[0] == B else m[None]
+        s = (s.reshape(B, Hq, L, T) + m).reshape(B, Hkv, G * L, T)
+    mx = s.amax(-1, keepdim=True)
+    e = torch.exp(s - mx)
+    l = e.sum(-1, keepdim=True)
+    acc = torch.matmul(e, value.float())                                  # [B, Hkv, G*L, Dv]
+    if partials is not None:
+        pr = partials.view(B, Hkv, G * L, 2 + Dv)
+        pr[..., 0:1] = mx
+        pr[..., 1:2] = l
+        pr[..., 2:] = acc
+    if not write_output:
+        return out
+    res = (acc / l).reshape(B, Hq, L, Dv).to(value.dtype)
+    if out is None:
+        return res
+    out.copy_(res)
     return out
 
 

@@ -48,6 +48,9 @@ CASES = {
     "g5_t1_g1": dict(cfg=CONFIGS["c1"].with_(q_heads=2, kv_heads=2, seq_len=1, dtype="bf16"),
                      scale="default", mask=None),
     # query_len 2 (non-causal) and a 3-D per-head mask, G=8
+    # block_dim 2 (the reference's default 4 bits/dim): 64 blocks per head at head_dim 128
+    "g9_bd2": dict(cfg=CONFIGS["c2"].with_(batch=1, q_heads=8, kv_heads=2, seq_len=300, block_dim=2),
+                   scale="default", mask="2d"),
     "g6_qlen2_mask3d": dict(cfg=CONFIGS["c5"].with_(batch=1, q_heads=16, kv_heads=2, seq_len=129,
                                                     head_dim=64, query_len=2),
                             scale="default", mask="3d"),

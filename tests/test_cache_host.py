@@ -92,3 +92,18 @@ def test_reference_names_without_calibration_raise_with_reason():
     assert require_triton_fast_path is require_fast_path
     with pytest.raises(NotImplementedError, match="offline calibration"):
         SunShapeCache.from_traces({}, [0], num_layers=1)
+
+
+def test_compressed_cache_builds_and_registers_attention():
+    import torch
+    from transformers import AttentionInterface
+
+    from sunshape_b200.compressed_cache import ATTN_IMPLEMENTATION, SunShapeCompressedCache, SunShapeCompressedLayer
+    from tests.helpers import make_codec
+
+    codec = make_codec(torch.arange(64), torch.zeros(8, 256, 8), torch.zeros(8, dtype=torch.bool), 64, 8, 256, "cpu")
+    cache = SunShapeCompressedCache.from_codecs({1: codec}, num_layers=3)
+    assert isinstance(cache.layers[1], SunShapeCompressedLayer)
+    assert not isinstance(cache.layers[0], SunShapeCompressedLayer)
+    assert cache.get_seq_length(1) == 0
+    assert ATTN_IMPLEMENTATION in AttentionInterface._global_mapping

@@ -145,6 +145,10 @@ SEEDED = {
     "t_short": CONFIGS["c2"].with_(batch=3, kv_heads=2, q_heads=4, seq_len=5),
     "qlen3": CONFIGS["c2"].with_(batch=1, kv_heads=2, q_heads=4, seq_len=300, query_len=3),
     "dv64_g1": CONFIGS["c1"].with_(q_heads=2, kv_heads=2, seq_len=1000, dtype="bf16"),
+    # block_dim 2 (64 blocks per head, the reference's default 4 bits/dim): fp16-entry LUTs, 4 rows per launch
+    "bd2_g8": CONFIGS["c5"].with_(batch=2, kv_heads=2, q_heads=16, seq_len=5000 + 3, block_dim=2),
+    "bd2_mixed": CONFIGS["c4"].with_(batch=1, kv_heads=2, q_heads=8, seq_len=3000, block_dim=2, n_heavy=8),
+    "bd2_fp32": CONFIGS["c1"].with_(head_dim=128, seq_len=2000, block_dim=2),
 }
 
 
@@ -156,7 +160,7 @@ def test_decode_matches_oracle_seeded(name):
                        cfg.n_centroids, DEV)
     qk = vab.quantize_codec_keys(codec, case["keys"])
     mask = None
-    if name in ("c2_ragged", "qlen3"):
+    if name in ("c2_ragged", "qlen3", "bd2_fp32"):
         gen = torch.Generator(device=DEV).manual_seed(3)
         mask = torch.randn(cfg.batch, cfg.q_heads, cfg.query_len, cfg.seq_len, device=DEV, generator=gen)
         mask[..., ::5] = float("-inf")
@@ -283,12 +287,12 @@ def test_split_kv_partials_merge_equals_full():
 
 
 def test_unsupported_inputs_raise_with_reason():
-    codec = make_codec(torch.randperm(128), torch.randn(1, 64, 256, 2), torch.zeros(64, dtype=torch.bool), 128, 2,
+    codec = make_codec(torch.randperm(256), torch.randn(1, 128, 256, 2), torch.zeros(128, dtype=torch.bool), 256, 2,
                        256, DEV)
-    q = torch.randn(1, 4, 1, 128, device=DEV, dtype=torch.bfloat16)
-    v = torch.randn(1, 1, 10, 128, device=DEV, dtype=torch.bfloat16)
-    keys = vab.SunShapeQuantizedKeys((), 1, 1, 10, indices=torch.zeros(1, 1, 10, 64, dtype=torch.uint8, device=DEV))
-    with pytest.raises(RuntimeError, match="n_blocks > 32"):
+    q = torch.randn(1, 4, 1, 256, device=DEV, dtype=torch.bfloat16)
+    v = torch.randn(1, 1, 10, 256, device=DEV, dtype=torch.bfloat16)
+    keys = vab.SunShapeQuantizedKeys((), 1, 1, 10, indices=torch.zeros(1, 1, 10, 128, dtype=torch.uint8, device=DEV))
+    with pytest.raises(RuntimeError, match="n_blocks > 64"):
         vab._apply_quantized_attention(codec=codec, query=q, key=keys, value=v, attn_mask=None, scale=None)
 
 
