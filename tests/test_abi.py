@@ -53,10 +53,10 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     # query heads not divisible by kv heads
     _expect(lib.sunshape_decode_attention(ctypes.byref(cd), ctypes.byref(kd), 16, 1, 1, 6, 4, 1, None, 0, 0, 0, 0,
                                           float("nan"), 16, 1, None, 16, 1 << 20, None), -1, "divisible by kv-head")
-    # more than 32 blocks is outside the fused LUT kernel
-    cd2 = _lib.CodecDesc(16, 16, None, 1, 128, 2, 256, 0, None)
+    # more than 64 blocks is outside the fused LUT kernel
+    cd2 = _lib.CodecDesc(16, 16, None, 1, 256, 2, 256, 0, None)
     _expect(lib.sunshape_decode_attention(ctypes.byref(cd2), ctypes.byref(kd), 16, 1, 1, 4, 4, 1, None, 0, 0, 0, 0,
-                                          float("nan"), 16, 1, None, 16, 1 << 20, None), -2, "n_blocks > 32")
+                                          float("nan"), 16, 1, None, 16, 1 << 20, None), -2, "n_blocks > 64")
     # misaligned value buffer
     kd_bad = _lib.KVDesc(16, 3, None, 1, 24, 1, 64, 10, 10)
     _expect(lib.sunshape_decode_attention(ctypes.byref(cd), ctypes.byref(kd_bad), 16, 1, 1, 4, 4, 1, None, 0, 0, 0,
