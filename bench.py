@@ -372,11 +372,11 @@ def run_ours(args, cfg: DecodeConfig):
         def step():
             vab._apply_quantized_attention(codec=codec, query=query, key=keys, value=value, attn_mask=None,
                                            scale=scale, out=out)
-        launches_per_step = 3   # lut_kernel + decode_mma_kernel + merge_slots_kernel
+        launches_per_step = 2   # lut_kernel + decode_mma_kernel
     else:
         def step():
             sharded(query, keys, value, scale=scale)
-        launches_per_step = 4   # lut_kernel + decode_mma_kernel + merge_slots_kernel + merge (or xmerge); NCCL not counted
+        launches_per_step = 3   # lut_kernel + decode_mma_kernel + merge / exchange kernel; NCCL not counted
 
     # decode kernel alone (events around the launch on its stream) for the roofline
     def kernel_only():

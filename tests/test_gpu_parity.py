@@ -147,7 +147,7 @@ SEEDED = {
     "dv64_g1": CONFIGS["c1"].with_(q_heads=2, kv_heads=2, seq_len=1000, dtype="bf16"),
     # block_dim 2 (64 blocks per head, the reference's default 4 bits/dim): fp16-entry LUTs, 4 rows per launch
     "bd2_g8": CONFIGS["c5"].with_(batch=2, kv_heads=2, q_heads=16, seq_len=5000 + 3, block_dim=2),
-    "bd2_mixed": CONFIGS["c4"].with_(batch=1, kv_heads=2, q_heads=8, seq_len=3000, block_dim=2, n_heavy=4),
+    "bd2_mixed": CONFIGS["c4"].with_(batch=1, kv_heads=2, q_heads=8, seq_len=3000, block_dim=2, n_heavy=2),
     "bd2_fp32": CONFIGS["c1"].with_(head_dim=128, seq_len=2000, block_dim=2),
 }
 
