@@ -26,7 +26,7 @@ __all__ = [
     "compact_index_dtype", "invert_permutation", "cdist_mm_fp32", "exact_block_distances",
     "quantize", "dequantize", "attention_scores", "query_centroid_lut",
     "lut_scores", "apply_quantized_attention", "merge_partials", "bf16_round",
-    "index_mismatches_are_ties",
+    "index_mismatches_are_ties", "metric_transform",
 ]
 
 
@@ -94,13 +94,32 @@ def exact_block_distances(keys_perm_block: np.ndarray, cents_block: np.ndarray) 
     return (diff * diff).sum(-1)
 
 
+def metric_transform(keys_perm: np.ndarray, centroids: np.ndarray, E: np.ndarray):
+    """SunShape-Pro (profileperm_localmetric_dsq) distance space, codec.py:375-377: key block b and the
+    block's codewords both multiplied by the metric block E[b*bd:(b+1)*bd, b*bd:(b+1)*bd] (transposed)
+    in fp32.  Returns (transformed keys [T, D], transformed codebooks [nb, C, bd])."""
+    nb, C, bd = centroids.shape
+    kt = np.empty_like(keys_perm, dtype=np.float32)
+    ct = np.empty_like(centroids, dtype=np.float32)
+    for b in range(nb):
+        sl = slice(b * bd, (b + 1) * bd)
+        eb = np.asarray(E[sl, sl], dtype=np.float32)
+        kt[:, sl] = keys_perm[:, sl].astype(np.float32) @ eb.T
+        ct[b] = centroids[b].astype(np.float32) @ eb.T
+    return kt, ct
+
+
 def quantize(keys: np.ndarray, perm: np.ndarray, centroids: np.ndarray,
-             heavy_mask: np.ndarray | None = None):
-    """SunShapeBlockCodec.quantize, codec.py:362-385 (E = I for the ProfilePerm modes).
+             heavy_mask: np.ndarray | None = None, E: np.ndarray | None = None):
+    """SunShapeBlockCodec.quantize, codec.py:362-385 (E = I for the ProfilePerm modes; the
+    SunShape-Pro metric E when given, compared in the transformed space, codec.py:375-377).
 
     keys [T, D] -> (indices [T, nb] compact dtype, passthrough [T, nb, bd] fp32 or None).
     Heavy (Mixed) blocks copy the permuted keys into the passthrough tensor and keep index 0.
     """
+    if E is not None:
+        kt, ct = metric_transform(np.asarray(keys, dtype=np.float32)[:, perm], centroids, E)
+        return quantize(kt, np.arange(kt.shape[1]), ct, heavy_mask)
     keys = np.asarray(keys, dtype=np.float32)
     nb, C, bd = centroids.shape
     kp = keys[:, perm]                                        # codec.py:247-252

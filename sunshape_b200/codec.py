@@ -53,8 +53,9 @@ class SunShapeBlockCodec(torch.nn.Module):
     """Block VQ key codec (ProfilePerm + per-block codebooks), CUDA-backed.
 
     Constructor arguments mirror ``sunshape/codec.py:205-216``.  Supported on the
-    CUDA path: the ProfilePerm modes with an identity metric ``E`` (``profileperm_baseline``,
-    ``profileperm_mixed_precision``) and ``identity_baseline``; other modes raise.
+    CUDA path: the ProfilePerm modes (``profileperm_baseline``, ``profileperm_mixed_precision``,
+    and SunShape-Pro ``profileperm_localmetric_dsq``, whose block-diagonal metric ``E`` changes only
+    the encode's distance) and ``identity_baseline``; ``rotated`` / ``legacy_strict`` raise.
     """
 
     def __init__(self, head_dim: int, block_dim: int = 8, n_centroids: int = 256, c: float = 5.0,
@@ -90,6 +91,7 @@ class SunShapeBlockCodec(torch.nn.Module):
         self.register_buffer("inv_permutation", ident.clone())
         self.register_buffer("rotation", torch.eye(head_dim, device=dev))
         self._desc_cache = None
+        self._metric_cache = None
 
     # ------------------------------------------------------------------ state
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
@@ -98,16 +100,19 @@ class SunShapeBlockCodec(torch.nn.Module):
             self.centroids = torch.empty_like(state_dict[key], device=self.centroids.device)
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
         self._desc_cache = None
+        self._metric_cache = None
 
     def _apply(self, fn, *args, **kwargs):
         out = super()._apply(fn, *args, **kwargs)
         self.device = self.E.device
         self._desc_cache = None
+        self._metric_cache = None
         return out
 
     def invalidate(self) -> None:
-        """Call after editing buffers in place (centroids, permutation, heavy mask)."""
+        """Call after editing buffers in place (centroids, permutation, heavy mask, metric)."""
         self._desc_cache = None
+        self._metric_cache = None
 
     @property
     def n_codebooks(self) -> int:
@@ -117,11 +122,36 @@ class SunShapeBlockCodec(torch.nn.Module):
     def is_mixed(self) -> bool:
         return self.mode == "profileperm_mixed_precision"
 
+    @property
+    def is_metric(self) -> bool:
+        """SunShape-Pro: nearest codeword under a block-diagonal local metric E (codec.py:375-377)."""
+        return self.mode == "profileperm_localmetric_dsq"
+
     def _check_supported(self) -> None:
-        if self.mode in ("rotated", "legacy_strict", "profileperm_localmetric_dsq"):
+        if self.mode in ("rotated", "legacy_strict"):
             raise RuntimeError(
                 f"mode {self.mode!r} uses a dense metric/rotation; the B200 kernels implement the ProfilePerm "
-                "modes with E = I (profileperm_baseline, profileperm_mixed_precision) and identity_baseline.")
+                "modes (profileperm_baseline, profileperm_mixed_precision, profileperm_localmetric_dsq) and "
+                "identity_baseline.")
+
+    def _metric_blocks(self) -> torch.Tensor:
+        """Diagonal blocks E_b [nb, bd, bd] of the SunShape-Pro metric (permuted basis)."""
+        bd, nb = self.block_dim, self.n_blocks
+        e = self.E.float().view(nb, bd, nb, bd)
+        return torch.stack([e[b, :, b, :] for b in range(nb)])
+
+    def _metric_desc(self):
+        """Encoder descriptor in the metric space: codewords C_b E_b^T, identity permutation."""
+        dc = getattr(self, "_metric_cache", None)
+        if dc is not None:
+            return dc
+        desc, keep, n_heavy = self.kernel_desc()
+        cents = keep[0]                                                        # [n_cb, nb, C, bd]
+        ct = torch.einsum("hbcd,bed->hbce", cents, self._metric_blocks()).contiguous()
+        ident = torch.arange(self.head_dim, device=cents.device, dtype=torch.int64)
+        mdesc = _lib.codec_desc(ct, ident, None, 0, self.head_dim, self.block_dim, None)
+        self._metric_cache = (mdesc, (ct, ident))
+        return self._metric_cache
 
     def kernel_desc(self):
         """C-ABI codec descriptor plus the tensors it points into (kept alive together)."""
@@ -203,7 +233,14 @@ class SunShapeBlockCodec(torch.nn.Module):
             hdt = heavy_dtype or (torch.bfloat16 if keys.dtype == torch.bfloat16 else torch.float32)
             heavy = torch.empty(*lead, T, n_heavy, self.block_dim, dtype=hdt, device=keys.device)
         if n_heads and T:
-            _lib.encode(desc, k, n_heads, kv_heads, T, k.stride(0), k.stride(1), idx, heavy, T)
+            if self.is_metric:
+                # SunShape-Pro: compare in the metric space -- key blocks (permuted) times E_b^T, one
+                # fp32 GEMM over the block-diagonal E, then the encoder against the transformed codebooks
+                mdesc, _ = self._metric_desc()
+                kt = torch.matmul(k.float()[..., self.permutation], self.E.float().t()).contiguous()
+                _lib.encode(mdesc, kt, n_heads, kv_heads, T, kt.stride(0), kt.stride(1), idx, None, T)
+            else:
+                _lib.encode(desc, k, n_heads, kv_heads, T, k.stride(0), k.stride(1), idx, heavy, T)
         return idx, heavy
 
     def _require_head(self, kv_head: int | None, what: str) -> int | None:

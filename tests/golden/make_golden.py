@@ -51,6 +51,9 @@ CASES = {
     # block_dim 2 (the reference's default 4 bits/dim): 64 blocks per head at head_dim 128
     "g9_bd2": dict(cfg=CONFIGS["c2"].with_(batch=1, q_heads=8, kv_heads=2, seq_len=300, block_dim=2),
                    scale="default", mask="2d"),
+    # SunShape-Pro: block-diagonal local metric E (codec.py:375-377), per-KV-head codebooks
+    "g10_pro_metric": dict(cfg=CONFIGS["c2"].with_(batch=1, q_heads=8, kv_heads=2, seq_len=400),
+                           scale="default", mask=None, metric=True),
     "g6_qlen2_mask3d": dict(cfg=CONFIGS["c5"].with_(batch=1, q_heads=16, kv_heads=2, seq_len=129,
                                                     head_dim=64, query_len=2),
                             scale="default", mask="3d"),
@@ -88,6 +91,15 @@ def run_case(name, spec):
     B, Hq, Hkv, D, T = cfg.batch, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.seq_len
     G = cfg.group
     mode = "profileperm_mixed_precision" if cfg.n_heavy else "profileperm_baseline"
+    E = None
+    if spec.get("metric"):
+        mode = "profileperm_localmetric_dsq"
+        gm = torch.Generator().manual_seed(9)
+        bd = cfg.block_dim
+        E = torch.zeros(D, D)
+        for b in range(cfg.n_blocks):
+            a = torch.randn(bd, bd, generator=gm) * 0.3
+            E[b * bd:(b + 1) * bd, b * bd:(b + 1) * bd] = torch.eye(bd) + 0.5 * (a + a.T)
 
     codecs = []
     for h in range(Hkv):
@@ -97,6 +109,9 @@ def run_case(name, spec):
         codec.inv_permutation.copy_(case["inv_perm"])
         codec.centroids.copy_(case["centroids"][h])
         codec.mixed_high_precision_blocks.copy_(case["heavy_mask"])
+        if E is not None:
+            codec.E.copy_(E)
+            codec.E_inv.copy_(torch.linalg.pinv(E))
         codecs.append(codec)
 
     nb, bd = cfg.n_blocks, cfg.block_dim
@@ -138,6 +153,7 @@ def run_case(name, spec):
         query=f32(case["query"]), value=f32(case["value"]),
         mask=np.zeros(0, np.float32) if mask is None else f32(mask),
         ref_indices=indices, ref_passthrough=passthrough, ref_scores=scores, ref_out=f32(out),
+        **({"E": E.numpy()} if E is not None else {}),
     )
     path = os.path.join(HERE, f"{name}.npz")
     np.savez_compressed(path, **payload)

@@ -27,21 +27,35 @@ def load_golden(name: str) -> dict:
     s = float(g["scale"])
     g["scale"] = None if np.isnan(s) else s
     g["mask"] = g["mask"] if g["mask"].size else None
+    g["E"] = g.get("E")            # SunShape-Pro local metric (block-diagonal [D, D]) or None
     return g
+
+
+def tie_space(keys_perm, centroids, E=None):
+    """(keys, codebooks) in the space the reference measures distances in: as given, or transformed by
+    the SunShape-Pro metric blocks (codec.py:375-377)."""
+    if E is None:
+        return keys_perm, centroids
+    from oracle import sunshape_oracle as O
+
+    return O.metric_transform(keys_perm, centroids, E)
 
 
 def torch_dtype(name: str):
     return {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[name]
 
 
-def make_codec(perm, centroids, heavy_mask, head_dim, block_dim, n_centroids, device):
-    """SunShapeBlockCodec with per-KV-head codebooks written directly (no fitting)."""
+def make_codec(perm, centroids, heavy_mask, head_dim, block_dim, n_centroids, device, E=None):
+    """SunShapeBlockCodec with per-KV-head codebooks written directly (no fitting); with ``E`` (a
+    block-diagonal [D, D] metric) a SunShape-Pro codec."""
     from sunshape_b200.codec import SunShapeBlockCodec
 
     perm = torch.as_tensor(perm, dtype=torch.long).cpu()
     cents = torch.as_tensor(centroids, dtype=torch.float32).cpu()
     heavy = torch.as_tensor(heavy_mask, dtype=torch.bool).cpu()
     mode = "profileperm_mixed_precision" if bool(heavy.any()) else "profileperm_baseline"
+    if E is not None:
+        mode = "profileperm_localmetric_dsq"
     codec = SunShapeBlockCodec(head_dim=head_dim, block_dim=block_dim, n_centroids=n_centroids, mode=mode,
                                device=torch.device(device), kv_heads=cents.shape[0] if cents.ndim == 4 else None)
     codec.permutation.copy_(perm)
@@ -50,6 +64,10 @@ def make_codec(perm, centroids, heavy_mask, head_dim, block_dim, n_centroids, de
     codec.inv_permutation.copy_(inv)
     codec.centroids.copy_(cents)
     codec.mixed_high_precision_blocks.copy_(heavy)
+    if E is not None:
+        Et = torch.as_tensor(E, dtype=torch.float32)
+        codec.E.copy_(Et)
+        codec.E_inv.copy_(torch.linalg.pinv(Et))
     codec.invalidate()
     return codec
 

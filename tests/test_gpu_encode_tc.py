@@ -17,7 +17,7 @@ import torch
 from oracle import sunshape_oracle as O
 from sunshape_b200 import vllm_attn_backend as vab
 from sunshape_b200.workloads import CONFIGS, make_case
-from tests.helpers import GOLDEN_CASES, load_golden, make_codec
+from tests.helpers import GOLDEN_CASES, load_golden, make_codec, tie_space
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -36,13 +36,12 @@ def encode_path(path):
             os.environ["SUNSHAPE_ENCODE"] = old
 
 
-def _check_ties(keys, perm, centroids, heavy_mask, idx_a, idx_b, what):
+def _check_ties(keys, perm, centroids, heavy_mask, idx_a, idx_b, what, E=None):
     B, H = idx_a.shape[:2]
     for b in range(B):
         for h in range(H):
-            kp = keys[b, h][:, perm]
-            n_mis, n_bad = O.index_mismatches_are_ties(kp, centroids[h % centroids.shape[0]], idx_a[b, h],
-                                                       idx_b[b, h], heavy_mask)
+            kp, cents = tie_space(keys[b, h][:, perm], centroids[h % centroids.shape[0]], E)
+            n_mis, n_bad = O.index_mismatches_are_ties(kp, cents, idx_a[b, h], idx_b[b, h], heavy_mask)
             assert n_bad == 0, f"{what} (b={b}, h={h}): {n_mis} mismatches, {n_bad} not ties"
 
 
@@ -52,7 +51,8 @@ def test_tensor_core_encode_matches_oracle_on_golden_keys(name):
     """The golden keys rounded to bf16 (the dtype a model hands the encoder); the oracle, pinned by
     the same fixtures, gives the expected indices for those keys."""
     g = load_golden(name)
-    codec = make_codec(g["perm"], g["centroids"], g["heavy_mask"], g["D"], g["block_dim"], g["n_centroids"], DEV)
+    codec = make_codec(g["perm"], g["centroids"], g["heavy_mask"], g["D"], g["block_dim"], g["n_centroids"], DEV,
+                       E=g["E"])
     keys = torch.from_numpy(g["keys"]).to(DEV).to(torch.bfloat16)
     kb = keys.float().cpu().numpy()
     with encode_path("tensor_cores"):
@@ -62,10 +62,10 @@ def test_tensor_core_encode_matches_oracle_on_golden_keys(name):
     ref = np.empty(qk.indices.shape, dtype=np.int64)
     for b in range(g["B"]):
         for h in range(g["Hkv"]):
-            ref[b, h], pt = O.quantize(kb[b, h], g["perm"], g["centroids"][h], hm)
+            ref[b, h], pt = O.quantize(kb[b, h], g["perm"], g["centroids"][h], hm, E=g["E"])
             if hm.any():
                 np.testing.assert_array_equal(qk.heavy[b, h].float().cpu().numpy(), pt[:, hm.astype(bool)])
-    _check_ties(kb, g["perm"], g["centroids"], hm, qk.indices.cpu().numpy(), ref, name)
+    _check_ties(kb, g["perm"], g["centroids"], hm, qk.indices.cpu().numpy(), ref, name, E=g["E"])
 
 
 @pytest.mark.parametrize("cfg_name,dtype,seq_len,n_centroids,batch", [

@@ -7,14 +7,15 @@ from oracle import sunshape_oracle as O
 from sunshape_b200 import vllm_attn_backend as vab
 from sunshape_b200.kernels import _torch_attention_scores, sunshape_attention_scores
 from sunshape_b200.workloads import CONFIGS, make_case
-from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_rowwise, load_golden, make_codec, torch_dtype
+from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_rowwise, load_golden, make_codec, tie_space, torch_dtype
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
 def golden_codec(g):
-    return make_codec(g["perm"], g["centroids"], g["heavy_mask"], g["D"], g["block_dim"], g["n_centroids"], DEV)
+    return make_codec(g["perm"], g["centroids"], g["heavy_mask"], g["D"], g["block_dim"], g["n_centroids"], DEV,
+                      E=g["E"])
 
 
 def golden_keys(g):
@@ -42,8 +43,8 @@ def test_encode_matches_reference_indices(name):
     hm = g["heavy_mask"]
     for b in range(g["B"]):
         for h in range(g["Hkv"]):
-            kp = g["keys"][b, h][:, g["perm"]]
-            n_mis, n_bad = O.index_mismatches_are_ties(kp, g["centroids"][h], idx[b, h], g["ref_indices"][b, h], hm)
+            kp, cents = tie_space(g["keys"][b, h][:, g["perm"]], g["centroids"][h], g["E"])
+            n_mis, n_bad = O.index_mismatches_are_ties(kp, cents, idx[b, h], g["ref_indices"][b, h], hm)
             assert n_bad == 0, f"{name}: {n_mis} index mismatches, {n_bad} not exact-distance ties"
     if hm.any():
         ref_h = g["ref_passthrough"][:, :, :, hm.astype(bool)]

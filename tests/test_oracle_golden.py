@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 from oracle import sunshape_oracle as O
-from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_rowwise, load_golden
+from tests.helpers import GOLDEN_CASES, TOL_BF16, TOL_F32, assert_close_rowwise, load_golden, tie_space
 
 
 def _heads(g, indices, passthrough):
@@ -21,10 +21,10 @@ def test_oracle_quantize_matches_reference(name):
     hm = g["heavy_mask"]
     for b in range(g["B"]):
         for h in range(g["Hkv"]):
-            idx, pt = O.quantize(g["keys"][b, h], g["perm"], g["centroids"][h], hm)
+            idx, pt = O.quantize(g["keys"][b, h], g["perm"], g["centroids"][h], hm, E=g["E"])
             assert idx.dtype == np.uint8
-            kp = g["keys"][b, h][:, g["perm"]]
-            n_mis, n_bad = O.index_mismatches_are_ties(kp, g["centroids"][h], idx, g["ref_indices"][b, h], hm)
+            kp, cents = tie_space(g["keys"][b, h][:, g["perm"]], g["centroids"][h], g["E"])
+            n_mis, n_bad = O.index_mismatches_are_ties(kp, cents, idx, g["ref_indices"][b, h], hm)
             assert n_bad == 0, f"{n_mis} mismatches, {n_bad} not ties"
             if hm.any():
                 np.testing.assert_array_equal(pt, g["ref_passthrough"][b, h])
