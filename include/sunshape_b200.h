@@ -176,6 +176,24 @@ int sunshape_decode_attention_peers(const sunshape_codec_t* codec, const sunshap
                                     const sunshape_peer_group_t* group,
                                     void* workspace, int64_t workspace_bytes, void* stream);
 
+/* ---- Bit-packed and wide codeword indices.
+ * Packed format (the reference's packed-index kernel, triton_kernels.py:213-292, with uint8
+ * elements): row t holds ceil(n_blocks * bits / 8) bytes; block b is in byte b / (8 / bits) at bit
+ * offset (b % (8 / bits)) * bits.  sunshape_index_row_bytes gives the row size for index_bits 1, 2, 4
+ * (packed), 8 (uint8), 16 (int16) or 32 (int32).
+ * sunshape_pack_indices: uint8 indices [n_rows, n_blocks] -> packed rows (bits 1, 2 or 4).
+ * sunshape_attention_scores_packed: scores [n_heads, rows, seq_len] fp32 of query [n_heads, rows,
+ * head_dim] (model basis) against indices [n_heads, head_stride, row_bytes] of that format
+ * (replaces _sunshape_packed_scores_kernel, triton_kernels.py:213-292, and serves the int16 indices
+ * of codebooks above 256 codewords, codec.py:78-83).  rows <= 16; no heavy blocks. */
+int64_t sunshape_index_row_bytes(int32_t index_bits, int32_t n_blocks);
+int sunshape_pack_indices(const uint8_t* indices, int64_t n_rows, int32_t n_blocks, int32_t bits, uint8_t* packed,
+                          void* stream);
+int sunshape_attention_scores_packed(const sunshape_codec_t* codec, const void* indices, int32_t index_bits,
+                                     int32_t seq_len, int64_t head_stride, const void* query, int32_t query_dtype,
+                                     int32_t n_heads, int32_t kv_heads, int32_t rows, float* scores_out,
+                                     void* stream);
+
 /* ---- Cross-GPU merge of per-rank partials over NVLink peer memory (no reference counterpart).
  * Each rank allocates one buffer of sunshape_exchange_buffer_bytes(world, rows, value_dim) with
  * sunshape_peer_alloc and maps every other rank's with sunshape_peer_open.  sunshape_exchange_merge

@@ -31,7 +31,8 @@ EXPORTED_SYMBOLS = (
     "sunshape_peer_alloc", "sunshape_peer_open", "sunshape_peer_close", "sunshape_peer_free",
     "sunshape_decode_attention_peers", "sunshape_decode_workspace_min_bytes", "sunshape_encode_error",
     "sunshape_decode_attention_noalloc_error", "sunshape_exchange_buffer_bytes", "sunshape_exchange_merge",
-    "sunshape_exchange_error",
+    "sunshape_exchange_error", "sunshape_index_row_bytes", "sunshape_pack_indices",
+    "sunshape_attention_scores_packed",
 )
 
 
@@ -105,6 +106,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sunshape_exchange_merge.restype = ctypes.c_int
         lib.sunshape_exchange_error.argtypes = [vp, i32, i64, i32, ctypes.POINTER(ctypes.c_int32)]
         lib.sunshape_exchange_error.restype = ctypes.c_int
+        lib.sunshape_index_row_bytes.argtypes = [i32, i32]
+        lib.sunshape_index_row_bytes.restype = ctypes.c_int64
+        lib.sunshape_pack_indices.argtypes = [vp, i64, i32, i32, vp, vp]
+        lib.sunshape_pack_indices.restype = ctypes.c_int
+        lib.sunshape_attention_scores_packed.argtypes = [pc, vp, i32, i32, i64, vp, i32, i32, i32, i32, vp, vp]
+        lib.sunshape_attention_scores_packed.restype = ctypes.c_int
         lib.sunshape_merge_partials.argtypes = [vp, i32, i64, i32, vp, i32, vp]
         lib.sunshape_decode_attention_noalloc.argtypes = [pc, pk, vp, i32, i32, i32, i32, i32, vp, i32, i64, i64,
                                                           i64, f32, vp, i32, vp, vp]
@@ -304,3 +311,25 @@ def exchange_merge(parts: torch.Tensor, out: torch.Tensor, group: PeerGroupDesc)
         _check(load_library().sunshape_exchange_merge(ptr(parts), int(parts.shape[0]), int(parts.shape[1] - 2),
                                                       ctypes.byref(group), ptr(out), dtype_code(out),
                                                       stream_ptr(dev)))
+
+
+def pack_indices(indices: torch.Tensor, bits: int) -> torch.Tensor:
+    """uint8 indices [..., n_blocks] -> packed uint8 rows [..., ceil(n_blocks * bits / 8)]."""
+    dev = require_cuda(indices)
+    nb = int(indices.shape[-1])
+    lib = load_library()
+    rb = int(lib.sunshape_index_row_bytes(bits, nb))
+    idx = indices.contiguous()
+    out = torch.empty(*idx.shape[:-1], rb, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(lib.sunshape_pack_indices(ptr(idx), idx.numel() // nb, nb, bits, ptr(out), stream_ptr(dev)))
+    return out
+
+
+def attention_scores_packed(cd: CodecDesc, indices: torch.Tensor, index_bits: int, seq_len: int, head_stride: int,
+                            query: torch.Tensor, n_heads: int, kv_heads: int, rows: int, out: torch.Tensor) -> None:
+    dev = require_cuda(indices, query, out)
+    with torch.cuda.device(dev):
+        _check(load_library().sunshape_attention_scores_packed(
+            ctypes.byref(cd), ptr(indices), index_bits, seq_len, head_stride, ptr(query), dtype_code(query), n_heads,
+            kv_heads, rows, ptr(out), stream_ptr(dev)))

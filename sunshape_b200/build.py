@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_NAME = "libsunshape_b200.so"
 LIB_PATH = os.path.join(HERE, LIB_NAME)
 SOURCES = ["capi.cu", "decode_f32.cu", "decode_bf16.cu", "decode_f16.cu", "decode_scores.cu", "decode_mma_bf16.cu",
-           "decode_mma_f16.cu", "noalloc.cu", "peer.cu", "encode_tc.cu", "exchange.cu"]
+           "decode_mma_f16.cu", "noalloc.cu", "peer.cu", "encode_tc.cu", "exchange.cu", "packed.cu"]
 DEPS = SOURCES + ["common.cuh", "decode.cuh", "decode_mma.cuh", "encode.cuh", "encode_params.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

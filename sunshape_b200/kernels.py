@@ -33,8 +33,6 @@ def _fast_path_unavailable_reason(codec, query: torch.Tensor, quantized_key) -> 
         return f"Query head dim {query.shape[1]} does not match codec.head_dim {codec.head_dim}."
     if codec.centroids.ndim not in (3, 4):
         return f"Expected codec.centroids.ndim == 3, got {codec.centroids.ndim}."
-    if codec.n_centroids > 256:
-        return "The LUT kernels need uint8 indices (n_centroids <= 256)."
     if query.shape[0] > 16 * 64:
         return "At most 1024 query rows per call."
     return None
@@ -74,6 +72,10 @@ def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, 
     h = codec._require_head(kv_head, "sunshape_attention_scores")
     if h is not None:
         codec = codec._head_view(h)
+    if quantized_key.indices.dtype in (torch.int16, torch.int32):
+        # codebooks above 256 codewords store int16 / int32 indices (codec.py:78-83)
+        return _wide_or_packed_scores(codec, query, quantized_key.indices,
+                                      16 if quantized_key.indices.dtype == torch.int16 else 32)
     if codec.n_blocks > 32:
         # more than 32 blocks (block_dim 2, the reference's default 4 bits/dim): a per-query LUT would
         # outgrow shared memory, so scores are the reference's own formula (triton_kernels.py:300-311)
@@ -97,6 +99,41 @@ def sunshape_attention_scores_strict(codec, query: torch.Tensor, quantized_key, 
         rows = min(16, n_rows - r0)
         _lib.attention_scores(desc, kd, q[r0:r0 + rows], 1, 1, rows, None, out[r0:r0 + rows])
     return out
+
+
+def _wide_or_packed_scores(codec, query: torch.Tensor, indices: torch.Tensor, bits: int) -> torch.Tensor:
+    desc, keep, n_heavy = codec.kernel_desc()
+    if n_heavy:
+        raise RuntimeError("packed / wide index scores do not take SunShape-Mixed heavy blocks.")
+    q = query.contiguous()
+    if q.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        q = q.float()
+    idx = indices.contiguous()
+    n_rows, T = q.shape[0], idx.shape[0]
+    out = torch.empty(n_rows, T, device=q.device, dtype=torch.float32)
+    if n_rows == 0 or T == 0:
+        return out
+    for r0 in range(0, n_rows, 16):
+        rows = min(16, n_rows - r0)
+        _lib.attention_scores_packed(desc, idx, bits, T, T, q[r0:r0 + rows], 1, 1, rows, out[r0:r0 + rows])
+    return out
+
+
+def sunshape_attention_scores_packed(codec, query: torch.Tensor, packed: torch.Tensor, bits: int, *,
+                                     kv_head: int | None = None) -> torch.Tensor:
+    """Scores [num_query_heads, num_tokens] against bit-packed indices [num_tokens, row_bytes] (1, 2 or 4
+    bits per block; the reference's packed format, triton_kernels.py:213-292)."""
+    if not query.is_cuda or not packed.is_cuda:
+        raise RuntimeError("sunshape_b200 runs only on CUDA tensors (B200, sm_100a); there is no CPU fallback.")
+    h = codec._require_head(kv_head, "sunshape_attention_scores_packed")
+    if h is not None:
+        codec = codec._head_view(h)
+    return _wide_or_packed_scores(codec, query, packed, int(bits))
+
+
+def pack_indices(indices: torch.Tensor, bits: int) -> torch.Tensor:
+    """Bit-pack uint8 indices [..., n_blocks] at 1, 2 or 4 bits per block (on the GPU)."""
+    return _lib.pack_indices(indices.to(torch.uint8), int(bits))
 
 
 def sunshape_attention_scores(codec, query: torch.Tensor, quantized_key, *, kv_head: int | None = None) -> torch.Tensor:
@@ -124,4 +161,6 @@ __all__ = [
     "require_fast_path",
     "_torch_attention_scores",
     "_precompute_query_centroid_dots",
+    "sunshape_attention_scores_packed",
+    "pack_indices",
 ]
