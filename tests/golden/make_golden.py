@@ -246,6 +246,30 @@ def run_cache():
     print(f"g8_cache: wrote {os.path.getsize(path) / 1024:.0f} KiB")
 
 
+def run_turbo():
+    """The reference's TurboQuant-MSE (turbo_baseline.py:117-186) at 1, 2 and 3 bits: rotation,
+    indices, norms and compressed-key attention scores for seeded keys and queries."""
+    from sunshape.turbo_baseline import TurboQuantMSE
+
+    g = torch.Generator().manual_seed(71)
+    d = 128
+    x = torch.randn(300, d, generator=g) * 0.7
+    q = torch.randn(8, d, generator=g)
+    payload = {"x": x.numpy(), "q": q.numpy()}
+    for bits in (1, 2, 3):
+        tq = TurboQuantMSE(d, bits=bits, seed=5 + bits, device=torch.device("cpu"))
+        comp = tq.compress(x)
+        payload[f"b{bits}_rotation"] = tq.rotation.numpy()
+        payload[f"b{bits}_centroids"] = tq.centroids.numpy()
+        payload[f"b{bits}_indices"] = comp.indices.numpy().astype(np.uint8)
+        payload[f"b{bits}_norms"] = comp.qjl_norms.numpy()
+        payload[f"b{bits}_scores"] = tq.attention_scores(q, comp).numpy()
+        payload[f"b{bits}_roundtrip"] = tq(x).numpy()
+    path = os.path.join(HERE, "g11_turbo.npz")
+    np.savez_compressed(path, **payload)
+    print(f"g11_turbo: wrote {os.path.getsize(path) / 1024:.0f} KiB")
+
+
 if __name__ == "__main__":
     import sunshape  # noqa: F401  (must resolve to the reference checkout)
     which = set(sys.argv[1:])
@@ -257,3 +281,5 @@ if __name__ == "__main__":
         run_bundle()
     if not which or "cache" in which:
         run_cache()
+    if not which or "turbo" in which:
+        run_turbo()

@@ -81,7 +81,9 @@ def test_turbo_cache_routes_flattened_fp32_keys_through_quantizer():
     assert k1.dtype == torch.bfloat16 and torch.equal(k1, -k) and torch.equal(v1, v)
     assert cache.get_seq_length(1) == 3 and not cache.has_previous_state()   # layer 0 decides, as in the reference
     with pytest.raises(NotImplementedError):
-        TurboQuantCache.for_layers(head_dims={0: 64}, layers=[0], num_layers=1)
+        TurboQuantCache.for_layers(head_dims={0: 64}, layers=[0], num_layers=1, mode="turboquant_prod")
+    built = TurboQuantCache.for_layers(head_dims={0: 64}, layers=[0], num_layers=1, device=torch.device("cpu"))
+    assert isinstance(built.layers[0], TurboQuantLayer) and built.layers[0].quantizer.bits == 3
     with pytest.raises(ValueError):
         TurboQuantCache(num_layers=None)
 
