@@ -537,8 +537,14 @@ def run_extra_configs(args):
     dev = torch.device("cuda", 0)
     peak, _ = measured_peaks()
     extra = {}
-    for name in ("c2", "c3", "c4"):
-        cfg = CONFIGS[name]
+    for name in ("c2", "c3", "c4", "c5_fp32_lut", "c2_bd2"):
+        if name == "c5_fp32_lut":      # the headline shape with fp32 LUT entries (fewer pipeline stages)
+            cfg = CONFIGS["c5"]
+            os.environ["SUNSHAPE_LUT_FP32"] = "1"
+        elif name == "c2_bd2":         # block_dim 2: the reference's default 4 bits/dim, 64 blocks per head
+            cfg = CONFIGS["c2"].with_(block_dim=2)
+        else:
+            cfg = CONFIGS[name]
         codec, idx, heavy, value, query, scale, Tl = build_shard(cfg, 0, 1, dev)
         keys = vab.SunShapeQuantizedKeys((), cfg.batch, cfg.kv_heads, Tl, indices=idx, heavy=heavy,
                                          passthrough_blocks=codec.mixed_high_precision_blocks if cfg.n_heavy else None)
@@ -550,6 +556,7 @@ def run_extra_configs(args):
         n = 100
         ms = time_steps(step, n, 5, torch.cuda.current_stream(dev)) / n
         alg = algorithmic_bytes(cfg, Tl)
+        os.environ.pop("SUNSHAPE_LUT_FP32", None)
         extra[name] = {"kv_tokens_per_s": cfg.kv_tokens() / (ms * 1e-3), "ms_per_step": ms,
                        "hbm_gbs": alg / (ms * 1e-3) / 1e9, "frac": alg / (ms * 1e-3) / 1e9 / peak}
         if name == "c3":
@@ -561,18 +568,19 @@ def run_extra_configs(args):
             byt = nkeys * (cfg.head_dim * 4 + cfg.n_blocks)
             extra["c3_encode"] = {"keys_per_s": nkeys / (ms_e * 1e-3), "ms": ms_e, "hbm_gbs": byt / (ms_e * 1e-3) / 1e9,
                                   "argmin_compares_per_s": nkeys * cfg.n_blocks * cfg.n_centroids / (ms_e * 1e-3),
-                                  "kernel": "encode_kernel (fp32 keys, CUDA cores)"}
+                                  "kernel": "encode_tc_kernel (fp32 keys, 3xTF32 on tcgen05, TMA key tiles)"}
             # bf16 keys (what a model hands the encoder): the tcgen05 kernel, 3 tf32 MMAs per block
             kb = kk.to(torch.bfloat16)
             del kk
             ms_b = time_steps(lambda: codec.quantize_packed(kb, kv_heads=cfg.kv_heads), 5, 2,
                               torch.cuda.current_stream(dev)) / 5
-            flops = 2.0 * nkeys * cfg.n_blocks * cfg.n_centroids * 24
+            kw = 16 if 2 * cfg.block_dim + 3 <= 16 else 32     # MMA K per block (tf32 words)
+            flops = 2.0 * nkeys * cfg.n_blocks * cfg.n_centroids * kw
             extra["c3_encode_bf16"] = {"keys_per_s": nkeys / (ms_b * 1e-3), "ms": ms_b,
                                        "hbm_gbs": nkeys * (cfg.head_dim * 2 + cfg.n_blocks) / (ms_b * 1e-3) / 1e9,
                                        "argmin_compares_per_s": nkeys * cfg.n_blocks * cfg.n_centroids / (ms_b * 1e-3),
                                        "tf32_tflops": flops / (ms_b * 1e-3) / 1e12,
-                                       "kernel": "encode_tc_kernel (tcgen05 kind::tf32, TMEM accumulator)"}
+                                       "kernel": "encode_tc_kernel (bf16 keys on tcgen05, TMA key tiles)"}
             del kb
         del codec, idx, heavy, value, query, keys, out
         torch.cuda.empty_cache()

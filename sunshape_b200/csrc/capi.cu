@@ -289,7 +289,10 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
     const int stages = std::min(kMaxStages, (kSmemLimit - 1024 - off_stage) / stage_bytes) / kTileGroupsM *
                        kTileGroupsM;
     const bool last = l16 == 1 || !l16_ok;
-    if (stages >= 8 || (last && stages >= kTileGroupsM)) {
+    // SUNSHAPE_LUT_FP32=1 keeps fp32 LUT entries whenever they fit at all (for precision comparisons)
+    const char* f32env = std::getenv("SUNSHAPE_LUT_FP32");
+    const bool force_f32 = f32env && std::atoi(f32env) != 0 && l16 == 0;
+    if (stages >= 8 || ((last || force_f32) && stages >= kTileGroupsM)) {
       pl.lut16 = l16 == 1;
       pl.gp = gp;
       pl.chunk_rows = std::min(rows, gp);
