@@ -168,6 +168,24 @@ int pick_gp(int rows) { return rows <= 4 ? 4 : (rows <= 8 ? 8 : 16); }
 
 // Lay out shared memory and the split for one launch configuration.
 // Returns false if it cannot fit.
+
+// Virtual tiles charged per head boundary by the CTA partition (see tile_start in decode.cuh):
+// SUNSHAPE_SEG_GAP overrides the default, capped at one head's tiles.
+constexpr int kSegGapDefault = 16;   // measured on B200: c5 at T 16384 79.3 -> 76.2 us, T 131072 370.0 -> 368.5 us
+int seg_gap_tiles(int64_t tph) {
+  static const int env = [] {
+    const char* e = std::getenv("SUNSHAPE_SEG_GAP");
+    return e ? std::max(0, std::atoi(e)) : -1;
+  }();
+  return (int)std::min<int64_t>(env >= 0 ? env : kSegGapDefault, tph);
+}
+// Most heads one CTA's range can touch under that partition (sizes the per-CTA partial slots).
+int64_t max_segments(int64_t n_heads, int64_t tph, int64_t grid) {
+  const int64_t v = n_heads * tph + (n_heads - 1) * seg_gap_tiles(tph);
+  const int64_t per_cta = (v + grid - 1) / grid;   // real tiles of one CTA are at most its virtual span
+  return (per_cta + tph - 1) / tph + 1;
+}
+
 bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_heavy_max, int bd,
                  int hsize, bool scores_only, int n_heads, int T, int rows, std::string& why) {
   int gp = pick_gp(rows);
@@ -179,7 +197,7 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
   for (;;) {
     const int lut_bytes = nbh * 8 * C * gp * 4;
     // staging for the warp partials + the contributing-slot table of the cross-CTA merge
-    const int stg_bytes = scores_only ? 0 : kWarps * gp * (dv + 2) * 4 + 16 + 8 * num_sms();
+    const int stg_bytes = scores_only ? 0 : kWarps * gp * (dv + 2) * 4 + (kWarps + 2) * gp * 4 + 16 + 8 * num_sms();
     const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
     const int off_perm = 256;
     const int off_hslot = off_perm + round_up(D * 4, 16);
@@ -214,10 +232,10 @@ bool plan_decode(DecodePlan& pl, int nb, int C, int D, int dv, int vsize, int n_
       const int tph = (T + kTileTokens - 1) / kTileTokens;
       const int64_t total = (int64_t)n_heads * tph;
       pl.grid = std::min<int64_t>(num_sms(), total);
-      const int64_t per_cta = (total + pl.grid - 1) / pl.grid;
       p.tph = tph;
       p.total_tiles = total;
-      p.max_seg = (int)((per_cta + tph - 1) / tph + 1);
+      p.seg_gap = seg_gap_tiles(tph);
+      p.max_seg = (int)max_segments(n_heads, tph, pl.grid);
       const int64_t slots = pl.grid * p.max_seg * gp * (int64_t)(dv + 2) * 4;
       pl.ws_bytes = 256 + round_up(n_heads * 4, 256) + slots;
       return true;
@@ -271,7 +289,7 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
    for (int l16 = 0; l16 < (l16_ok ? 2 : 1); ++l16) {
     const int nt = (gp + 7) / 8;
     const int lut_bytes = nbh * 8 * kLutC * gp * (l16 ? 2 : 4);
-    const int stg_bytes = kWarpsM * gp * (dv + 2) * 4 + 16 + 8 * num_sms();
+    const int stg_bytes = kWarpsM * gp * (dv + 2) * 4 + (kWarpsM + 2) * gp * 4 + 16 + 8 * num_sms();
     const int region = round_up(std::max(lut_bytes, stg_bytes), 128);
     const int off_perm = 256;
     const int off_hslot = off_perm + round_up(D * 4, 16);
@@ -314,10 +332,10 @@ bool plan_decode_mma(DecodePlan& pl, int nb, int D, int dv, int n_heavy, int bd,
       const int tph = (T + kTileTokens - 1) / kTileTokens;
       const int64_t total = (int64_t)n_heads * tph;
       pl.grid = std::min<int64_t>(num_sms(), total);
-      const int64_t per_cta = (total + pl.grid - 1) / pl.grid;
       p.tph = tph;
       p.total_tiles = total;
-      p.max_seg = (int)((per_cta + tph - 1) / tph + 1);
+      p.seg_gap = seg_gap_tiles(tph);
+      p.max_seg = (int)max_segments(n_heads, tph, pl.grid);
       p.lut_bytes = lut_bytes;
       p.merge_smem_bytes = off_stage - off_lut;
       pl.ws_bytes = mma_workspace_bytes(n_heads, pl.grid, p.max_seg, gp, dv, 0);
@@ -611,8 +629,7 @@ int64_t sunshape_decode_workspace_bytes(int32_t n_heads, int32_t seq_len, int32_
   const int tph = (seq_len + kTileTokens - 1) / kTileTokens;
   const int64_t total = (int64_t)n_heads * tph;
   const int64_t grid = std::min<int64_t>(num_sms(), total);
-  const int64_t per_cta = (total + grid - 1) / grid;
-  const int64_t max_seg = (per_cta + tph - 1) / tph + 1;
+  const int64_t max_seg = max_segments(n_heads, tph, grid);
   // per-head LUT area: fp32 entries with a fixed 256-row stride (upper bound), within the policy cap
   const int64_t lut_bytes = (int64_t)((std::max(n_blocks, 1) + 7) / 8) * 8 * kLutC * gp * 4;
   return mma_workspace_bytes(n_heads, grid, max_seg, gp, value_dim,
@@ -625,8 +642,7 @@ int64_t sunshape_decode_workspace_min_bytes(int32_t n_heads, int32_t seq_len, in
   const int tph = (seq_len + kTileTokens - 1) / kTileTokens;
   const int64_t total = (int64_t)n_heads * tph;
   const int64_t grid = std::min<int64_t>(num_sms(), total);
-  const int64_t per_cta = (total + grid - 1) / grid;
-  const int64_t max_seg = (per_cta + tph - 1) / tph + 1;
+  const int64_t max_seg = max_segments(n_heads, tph, grid);
   return mma_workspace_bytes(n_heads, grid, max_seg, gp, value_dim, 0);
 }
 

@@ -105,6 +105,7 @@ struct DecodeParams {
   int tph;            // tiles per head
   int64_t total_tiles;
   int max_seg;
+  int seg_gap;        // virtual tiles charged per head boundary by the partition
   // shared memory carve-up (bytes)
   int stages;
   int prefetch_ahead;   // tiles streamed into L2 beyond the ring (tensor-core kernel)
@@ -114,12 +115,25 @@ struct DecodeParams {
   int off_perm, off_hslot, off_q, off_p, off_lut, off_stage;
 };
 
-__device__ __forceinline__ int64_t tile_start(int64_t c, int64_t total, int64_t grid) {
-  return c * total / grid;
+// Partition of the flattened (head, tile) space over the persistent CTAs.  Finishing a head in the
+// middle of a CTA's range costs that CTA time (merging the head's partials, loading the next head's
+// LUT), so the split is made over a virtual sequence in which every head boundary counts as seg_gap
+// extra tiles: CTAs whose range crosses a boundary get correspondingly fewer real tiles.  seg_gap = 0
+// is the plain equal split.
+__device__ __forceinline__ int64_t virtual_tiles(const DecodeParams& p) {
+  return p.total_tiles + (p.total_tiles / p.tph - 1) * p.seg_gap;
 }
-// the CTA whose tile range contains tile f
-__device__ __forceinline__ int64_t tile_owner(int64_t f, int64_t total, int64_t grid) {
-  return ((f + 1) * grid - 1) / total;
+// first real tile of CTA c (c = grid gives total_tiles)
+__device__ __forceinline__ int64_t tile_start(const DecodeParams& p, int64_t c, int64_t grid) {
+  const int64_t v = c * virtual_tiles(p) / grid;
+  const int64_t span = p.tph + p.seg_gap;
+  const int64_t h = v / span;
+  return h * p.tph + min(v - h * span, (int64_t)p.tph);
+}
+// the CTA whose tile range contains real tile f
+__device__ __forceinline__ int64_t tile_owner(const DecodeParams& p, int64_t f, int64_t grid) {
+  const int64_t vf = f + (f / p.tph) * p.seg_gap;
+  return ((vf + 1) * grid - 1) / virtual_tiles(p);
 }
 
 // rows held by lane j (0..7 within its token group) after the reduce-scatter
@@ -346,6 +360,54 @@ __device__ __forceinline__ void emit_row(const DecodeParams& p, int64_t orow, in
   }
 }
 
+// Four consecutive output columns d0..d0+3 of one merged row (d0 % 4 == 0): vector stores where the
+// destination is aligned (bf16/f16 outputs 8 bytes, fp32 16 bytes, partial rows 8 bytes), else scalar.
+template <int DV>
+__device__ __forceinline__ void emit_row4(const DecodeParams& p, int64_t orow, int d0, float M, float Lsum,
+                                          const float (&a)[4], unsigned parity) {
+  const float NEG_INF = -__int_as_float(0x7f800000);
+  if (p.out) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = M == NEG_INF ? __int_as_float(0x7fc00000) : a[j] / Lsum;
+    const int64_t i0 = orow * DV + d0;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(p.out);
+    if (p.out_dtype == SUNSHAPE_F32 && (addr & 15) == 0) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + i0) = make_float4(v[0], v[1], v[2], v[3]);
+    } else if (p.out_dtype == SUNSHAPE_BF16 && (addr & 7) == 0) {
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + i0) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    } else if (p.out_dtype == SUNSHAPE_F16 && (addr & 7) == 0) {
+      const __half2 lo = __floats2half2_rn(v[0], v[1]), hi = __floats2half2_rn(v[2], v[3]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + i0) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) store_from_float(p.out, i0 + j, p.out_dtype, v[j]);
+    }
+  }
+  auto put_row = [&](float* pr) {   // [m, l, acc...] row of DV + 2 floats
+    if ((reinterpret_cast<uintptr_t>(pr) & 7) == 0) {
+      reinterpret_cast<float2*>(pr + 2 + d0)[0] = make_float2(a[0], a[1]);
+      reinterpret_cast<float2*>(pr + 2 + d0)[1] = make_float2(a[2], a[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pr[2 + d0 + j] = a[j];
+    }
+    if (d0 == 0) { pr[0] = M; pr[1] = Lsum; }
+  };
+  if (p.partials) put_row(p.partials + orow * (int64_t)(DV + 2));
+  for (int r = 0; r < p.xworld; ++r)
+    put_row(p.xrecv[r] + ((int64_t)(parity * p.xworld + p.xrank) * p.x_rows + orow) * (DV + 2));
+}
+
+__device__ __forceinline__ int ld_relaxed_gpu(const int* a) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a));
+  return v;
+}
+
 // After every thread emitted its rows of head hh: make the peer stores visible system-wide, then
 // count this rank's arrival for hh on every rank.
 __device__ __forceinline__ void signal_peers(const DecodeParams& p, int64_t hh, unsigned parity, int ctid, int nt) {
@@ -361,122 +423,194 @@ __device__ __forceinline__ void signal_peers(const DecodeParams& p, int64_t hh, 
 #else
 #define SUNSHAPE_FMARK(k) ((void)0)
 #endif
+// End of one (head, CTA) segment.  stg holds NW per-warp partial rows [m, l, acc[DV]] per query row.
+// They are merged (log-sum-exp, fixed warp order) into this CTA's partial for head hh, which is
+//   * emitted directly when this CTA holds the whole head (sole);
+//   * otherwise combined with the other CTAs' partials of hh: the contributor that finds all others
+//     already counted (ticket == contributors - 1, read before it writes anything, then a fence)
+//     merges right away from shared memory and the others' slots; every other contributor writes
+//     its slot, fences and takes a ticket, and the one that draws the last ticket merges.
+// Shared memory after the staging rows: merge weights [NW][GP], row maxima [GP], row sums [GP], then the
+// contributors' slot offsets and (when they fit) the gathered slots.  Sums run in the same order as a
+// scalar merge (warps, then contributors in CTA order), so results do not depend on the vector width.
 template <int GP, int DV, int NW, bool PRECISE = false>
 __device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t hh, int64_t tb, int64_t grid,
                                int ctid, int* flag_s) {
   constexpr int ROWF = DV + 2;
   constexpr int NT = NW * 32;
+  constexpr int DV4 = DV / 4;
+  static_assert(DV % 4 == 0, "value_dim");
   const float NEG_INF = -__int_as_float(0x7f800000);
-  const int64_t c_first = tile_owner(hh * p.tph, p.total_tiles, grid);
-  const int64_t c_last = tile_owner((hh + 1) * p.tph - 1, p.total_tiles, grid);
+  const int64_t c_first = tile_owner(p, hh * p.tph, grid);
+  const int64_t c_last = tile_owner(p, (hh + 1) * p.tph - 1, grid);
   const bool sole = c_first == c_last;
+  const int n_contrib = (int)(c_last - c_first + 1);
   const int seg_local = (int)(hh - tb / p.tph);
   float* slot = p.slots + ((int64_t)blockIdx.x * p.max_seg + seg_local) * GP * ROWF;
   const unsigned parity = p.xworld ? (*reinterpret_cast<const volatile unsigned int*>(p.xstep) & 1u) : 0u;
-  for (int e = ctid; e < p.Rc * DV; e += NT) {
-    const int r = e / DV, d = e - r * DV;
+  float* const stgw = const_cast<float*>(stg);
+  float* wgt = stgw + NW * GP * ROWF;   // [NW][GP]
+  float* Ms = wgt + NW * GP;             // [GP]
+  float* Ls = Ms + GP;                   // [GP]
+  int64_t* offs = reinterpret_cast<int64_t*>(Ls + GP + 2);
+  float* gath = reinterpret_cast<float*>(offs + n_contrib);
+  const int slot_f = p.Rc * ROWF;
+  const bool fits = (int64_t)(reinterpret_cast<uint8_t*>(gath + (int64_t)n_contrib * slot_f) -
+                              reinterpret_cast<const uint8_t*>(stg)) <= p.merge_smem_bytes;
+  const int k_self = (int)(blockIdx.x - c_first);
+
+  // ---- per-row maxima and warp weights (one thread per row); the early ticket check of a split head
+  // (issued first so its latency overlaps the weights; the fence below orders the slot reads after it)
+  const int ticket_now = (ctid == 0 && !sole && fits) ? ld_relaxed_gpu(p.counters + hh) : -1;
+  if (ctid < p.Rc) {
+    const int r = ctid;
     float M = NEG_INF;
     for (int w = 0; w < NW; ++w) M = fmaxf(M, stg[(w * GP + r) * ROWF]);
-    float Lsum = 0.f, A = 0.f;
-    if (M != NEG_INF) {
-      for (int w = 0; w < NW; ++w) {
-        const float* src = stg + (w * GP + r) * ROWF;
-        const float sc = softmax_weight<PRECISE>(src[0] - M);
-        Lsum = fmaf(src[1], sc, Lsum);
-        A = fmaf(src[2 + d], sc, A);
-      }
+    float L = 0.f;
+    for (int w = 0; w < NW; ++w) {
+      const float* src = stg + (w * GP + r) * ROWF;
+      const float wt = M == NEG_INF ? 0.f : softmax_weight<PRECISE>(src[0] - M);
+      wgt[w * GP + r] = wt;
+      L = fmaf(src[1], wt, L);
     }
+    Ms[r] = M;
+    Ls[r] = L;
+  }
+  if (ctid == 0) {
+    const bool last = ticket_now == n_contrib - 1;
+    if (last) __threadfence();
+    flag_s[3] = last ? 1 : 0;
+  }
+  named_barrier(kBarConsumers, NT);
+  const bool last_now = flag_s[3] != 0;
+
+  // ---- this CTA's partial: 4 columns per thread
+  for (int e = ctid; e < p.Rc * DV4; e += NT) {
+    const int r = e / DV4, d0 = (e - r * DV4) * 4;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = 0; w < NW; ++w) {
+      const float wt = wgt[w * GP + r];
+      const float2* src = reinterpret_cast<const float2*>(stg + (w * GP + r) * ROWF + 2 + d0);
+      const float2 x0 = src[0], x1 = src[1];
+      a[0] = fmaf(x0.x, wt, a[0]); a[1] = fmaf(x0.y, wt, a[1]);
+      a[2] = fmaf(x1.x, wt, a[2]); a[3] = fmaf(x1.y, wt, a[3]);
+    }
+    const float M = Ms[r], L = Ls[r];
     if (sole) {
-      emit_row<DV>(p, hh * p.R + p.r0 + r, d, M, Lsum, A, parity);
+      emit_row4<DV>(p, hh * p.R + p.r0 + r, d0, M, L, a, parity);
     } else {
-      slot[r * ROWF + 2 + d] = A;
-      if (d == 0) { slot[r * ROWF] = M; slot[r * ROWF + 1] = Lsum; }
+      float* dst = last_now ? gath + (int64_t)k_self * slot_f + r * ROWF : slot + r * ROWF;
+      reinterpret_cast<float2*>(dst + 2 + d0)[0] = make_float2(a[0], a[1]);
+      reinterpret_cast<float2*>(dst + 2 + d0)[1] = make_float2(a[2], a[3]);
+      if (d0 == 0) { dst[0] = M; dst[1] = L; }
     }
   }
   SUNSHAPE_FMARK(8);
-  if (sole) signal_peers(p, hh, parity, ctid, NT);
-  if (!sole) {
+  if (sole) {
+    signal_peers(p, hh, parity, ctid, NT);
+    return;
+  }
+  if (!last_now) {
     __threadfence();
     SUNSHAPE_FMARK(9);
     named_barrier(kBarConsumers, NT);
     if (ctid == 0) {
-      const int n_contrib = (int)(c_last - c_first + 1);
       const int prev = atomicAdd(&p.counters[hh], 1);
       flag_s[0] = prev == n_contrib - 1;
     }
     named_barrier(kBarConsumers, NT);
     SUNSHAPE_FMARK(10);
-    if (flag_s[0]) {
-      __threadfence();
-      // float offsets of the contributing CTAs' slots for this head, computed once
-      int64_t* offs = reinterpret_cast<int64_t*>(const_cast<float*>(stg) + NW * GP * ROWF + 2);
-      const int n_contrib = (int)(c_last - c_first + 1);
-      for (int k = ctid; k < n_contrib; k += NT) {
-        const int64_t c = c_first + k;
-        const int sl = (int)(hh - tile_start(c, p.total_tiles, grid) / p.tph);
-        offs[k] = (c * p.max_seg + sl) * GP * ROWF;
-      }
-      named_barrier(kBarConsumers, NT);
-      SUNSHAPE_FMARK(12);
-      // merge the contributing CTAs' slots: when they fit, gather them into shared memory first
-      // (one batch of independent loads; the slots were written long ago and may sit in HBM),
-      // then reduce from shared memory
-      const int slot_f = p.Rc * ROWF;
-      float* gath = reinterpret_cast<float*>(offs + n_contrib);
-      const bool staged = (int64_t)(reinterpret_cast<uint8_t*>(gath + (int64_t)n_contrib * slot_f) -
-                                    reinterpret_cast<const uint8_t*>(stg)) <= p.merge_smem_bytes;
-      const float* base = p.slots;
-      SUNSHAPE_FMARK(21);
-#ifdef SUNSHAPE_TRACE
-      if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + 23] = clock64();
-#endif
-      if (staged) {
-        const int tot = n_contrib * slot_f;
-        for (int b0 = ctid; b0 < tot; b0 += NT * 8) {   // 8 loads in flight per thread
-          float v[8];
+    if (!flag_s[0]) return;
+  }
+  __threadfence();
+  // float offsets of the contributing CTAs' slots for this head
+  for (int k = ctid; k < n_contrib; k += NT) {
+    const int64_t c = c_first + k;
+    const int sl = (int)(hh - tile_start(p, c, grid) / p.tph);
+    offs[k] = (c * p.max_seg + sl) * GP * ROWF;
+  }
+  named_barrier(kBarConsumers, NT);
+  SUNSHAPE_FMARK(12);
+  if (fits) {
+    // gather the slots into shared memory in one batch of independent 8-byte loads (the slots were
+    // written by other SMs and may sit in HBM), skipping this CTA's own partial when it is already there
+    const int slot_h = slot_f / 2;
+    const int tot = n_contrib * slot_h;
+    for (int b0 = ctid; b0 < tot; b0 += NT * 8) {
+      float2 v[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int idx = b0 + u * NT;
-            const int k = idx / slot_f;
-            v[u] = idx < tot ? __ldcg(p.slots + offs[min(k, n_contrib - 1)] + (idx - k * slot_f)) : 0.f;
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            if (b0 + u * NT < tot) gath[b0 + u * NT] = v[u];
-        }
-        named_barrier(kBarConsumers, NT);
+      for (int u = 0; u < 8; ++u) {
+        const int idx = b0 + u * NT;
+        const int k = min(idx / slot_h, n_contrib - 1);
+        v[u] = (idx < tot && !(last_now && k == k_self))
+                   ? __ldcg(reinterpret_cast<const float2*>(p.slots + offs[k]) + (idx - k * slot_h))
+                   : make_float2(0.f, 0.f);
       }
-      SUNSHAPE_FMARK(22);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int idx = b0 + u * NT;
+        const int k = min(idx / slot_h, n_contrib - 1);
+        if (idx < tot && !(last_now && k == k_self)) reinterpret_cast<float2*>(gath)[idx] = v[u];
+      }
+    }
+    named_barrier(kBarConsumers, NT);
+    SUNSHAPE_FMARK(22);
+    // contributor weights per row (the staging rows are no longer needed: reuse them)
+    float* w2 = stgw;                       // [n_contrib][GP]
+    float* M2 = w2 + n_contrib * GP;        // [GP]
+    float* L2 = M2 + GP;                    // [GP]
+    if (ctid < p.Rc) {
+      const int r = ctid;
+      float M = NEG_INF;
+      for (int k = 0; k < n_contrib; ++k) M = fmaxf(M, gath[k * slot_f + r * ROWF]);
+      float L = 0.f;
+      for (int k = 0; k < n_contrib; ++k) {
+        const float* src = gath + k * slot_f + r * ROWF;
+        const float wt = M == NEG_INF ? 0.f : softmax_weight<PRECISE>(src[0] - M);   // empty slot -> 0
+        w2[k * GP + r] = wt;
+        L = fmaf(src[1], wt, L);
+      }
+      M2[r] = M;
+      L2[r] = L;
+    }
+    named_barrier(kBarConsumers, NT);
+    for (int e = ctid; e < p.Rc * DV4; e += NT) {
+      const int r = e / DV4, d0 = (e - r * DV4) * 4;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int k = 0; k < n_contrib; ++k) {
+        const float wt = w2[k * GP + r];
+        const float2* src = reinterpret_cast<const float2*>(gath + k * slot_f + r * ROWF + 2 + d0);
+        const float2 x0 = src[0], x1 = src[1];
+        a[0] = fmaf(x0.x, wt, a[0]); a[1] = fmaf(x0.y, wt, a[1]);
+        a[2] = fmaf(x1.x, wt, a[2]); a[3] = fmaf(x1.y, wt, a[3]);
+      }
+      emit_row4<DV>(p, hh * p.R + p.r0 + r, d0, M2[r], L2[r], a, parity);
+    }
+  } else {
+    // many contributors (long sequences over few heads): reduce straight from the slots
+    const float* base = p.slots;
 #pragma unroll 1
-      for (int e = ctid; e < p.Rc * DV; e += NT) {
-        const int r = e / DV, d = e - r * DV;
-        float M = NEG_INF;
-        for (int k = 0; k < n_contrib; ++k)
-          M = fmaxf(M, staged ? gath[k * slot_f + r * ROWF] : __ldcg(base + offs[k] + r * ROWF));
-        float Lsum = 0.f, A = 0.f;
-        if (M != NEG_INF) {
-          for (int k = 0; k < n_contrib; ++k) {
-            const float* src = staged ? gath + k * slot_f + r * ROWF : base + offs[k] + r * ROWF;
-            const float m = staged ? src[0] : __ldcg(src);
-            const float l = staged ? src[1] : __ldcg(src + 1);
-            const float a = staged ? src[2 + d] : __ldcg(src + 2 + d);
-            const float sc = softmax_weight<PRECISE>(m - M);   // m = -inf (empty slot) -> 0
-            Lsum = fmaf(l, sc, Lsum);
-            A = fmaf(a, sc, A);
-          }
+    for (int e = ctid; e < p.Rc * DV; e += NT) {
+      const int r = e / DV, d = e - r * DV;
+      float M = NEG_INF;
+      for (int k = 0; k < n_contrib; ++k) M = fmaxf(M, __ldcg(base + offs[k] + r * ROWF));
+      float Lsum = 0.f, A = 0.f;
+      if (M != NEG_INF) {
+        for (int k = 0; k < n_contrib; ++k) {
+          const float* src = base + offs[k] + r * ROWF;
+          const float sc = softmax_weight<PRECISE>(__ldcg(src) - M);
+          Lsum = fmaf(__ldcg(src + 1), sc, Lsum);
+          A = fmaf(__ldcg(src + 2 + d), sc, A);
         }
-        emit_row<DV>(p, hh * p.R + p.r0 + r, d, M, Lsum, A, parity);
       }
-      signal_peers(p, hh, parity, ctid, NT);
-      named_barrier(kBarConsumers, NT);
-      SUNSHAPE_FMARK(13);
-#ifdef SUNSHAPE_TRACE
-      if (ctid == 0 && p.trace) p.trace[blockIdx.x * 32 + 24] = clock64();
-#endif
-      if (ctid == 0) atomicExch(&p.counters[hh], 0);
-      SUNSHAPE_FMARK(11);
+      emit_row<DV>(p, hh * p.R + p.r0 + r, d, M, Lsum, A, parity);
     }
   }
+  signal_peers(p, hh, parity, ctid, NT);
+  named_barrier(kBarConsumers, NT);
+  SUNSHAPE_FMARK(13);
+  if (ctid == 0) atomicExch(&p.counters[hh], 0);
+  SUNSHAPE_FMARK(11);
 }
 
 template <int GP, int DV, typename VT, bool SCORES_ONLY>
@@ -499,8 +633,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t grid = gridDim.x;
-  const int64_t tb = tile_start(blockIdx.x, p.total_tiles, grid);
-  const int64_t te = tile_start(blockIdx.x + 1, p.total_tiles, grid);
+  const int64_t tb = tile_start(p, blockIdx.x, grid);
+  const int64_t te = tile_start(p, blockIdx.x + 1, grid);
 
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {

@@ -495,6 +495,7 @@ void launch_lut_t(const DecodeParams& prm, int n_heads, int n_sms, cudaStream_t 
 template <int GP, bool L16>
 __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ DecodeParams p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  SUNSHAPE_SPAN_START(0);
   __shared__ float q_s[GP * 256];
   __shared__ float red[2];
   const int tid = threadIdx.x;
@@ -573,6 +574,7 @@ __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ Decode
   uint8_t* dst = (L16 && GP == 4) ? base + (int64_t)(kh >> 1) * kLutC * 128 + blo * 16 + (kh & 1) * 8
                                   : base + (int64_t)kh * NH * kLutC * 128 + blo * 16;
   store_lut_entry<GP, L16>(dst, c, v, scale);
+  SUNSHAPE_SPAN_END(1);
 }
 
 template <int GP, bool L16>
@@ -708,8 +710,8 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t grid = gridDim.x;
-  const int64_t tb = tile_start(blockIdx.x, p.total_tiles, grid);
-  const int64_t te = tile_start(blockIdx.x + 1, p.total_tiles, grid);
+  const int64_t tb = tile_start(p, blockIdx.x, grid);
+  const int64_t te = tile_start(p, blockIdx.x + 1, grid);
 
   if (tid == 0) {
     SUNSHAPE_MARK(0);
