@@ -166,7 +166,10 @@ int sunshape_peer_free(void* dev_ptr);
  * (m, l, acc) rows into every rank's exchange buffer over NVLink and bumps that rank's per-head
  * arrival counter; a merge kernel waits (bounded) for all ranks' rows of each head and writes
  * out [batch, q_heads, query_len, value_dim].  All ranks must make the same sequence of calls.
- * Requires G * query_len <= 16 rows per KV head and 16-bit values. */
+ * Requires G * query_len <= 16 rows per KV head and 16-bit values.  Errors land in the workspace
+ * error word: 104 = the merge gave up waiting for a peer (that call's rows are NaN); the timeout
+ * also poisons this rank's exchange buffer, after which every call records 106 and writes NaN rows
+ * until the buffers are freed and a new group is set up. */
 int sunshape_decode_attention_peers(const sunshape_codec_t* codec, const sunshape_kv_t* kv,
                                     const void* query, int32_t query_dtype,
                                     int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t query_len,

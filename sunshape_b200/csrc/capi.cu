@@ -50,26 +50,46 @@ inline PeerLayout peer_layout(int world, int64_t rows, int dv, int n_heads) {
 // Cross-GPU merge: one CTA per KV head waits (bounded) until every rank's rows of the head have
 // arrived in this rank's exchange buffer, merges them in rank order and writes the output; the
 // last CTA advances the step counter (its parity selects the buffer half of the next call).
+// A wait that gives up (error 104) leaves the arrival counts out of step with the peers: a slow
+// rank's late arrivals would land in a half that is reused two calls later and be merged as if
+// current.  So a timeout also sets a sticky poison word (step + 2); while it is set every later
+// call records error 106 and writes NaN rows instead of merging, until the exchange buffers are
+// freed and allocated again (a new peer group).
 __global__ void xmerge_kernel(float* recv, unsigned int* arrive, unsigned int* step, unsigned int* done, int world,
                               int64_t rows, int R, int dv, int n_heads, void* out, int out_dtype, int* err) {
   __shared__ unsigned parity_s;
   const int64_t hh = blockIdx.x;
   const float NEG_INF = -__int_as_float(0x7f800000);
+  __shared__ int bad_s;
+  volatile unsigned int* poison = step + 2;
   if (threadIdx.x == 0) {
     const unsigned parity = *reinterpret_cast<volatile unsigned int*>(step) & 1u;
     parity_s = parity;
-    unsigned int* a = arrive + (int64_t)parity * n_heads + hh;
-    const uint64_t t0 = global_ns();
-    while (true) {
-      unsigned int v;
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
-      if ((int)v >= world) break;
-      if (global_ns() - t0 > kWaitLimitNs) { record_error(err, 104); break; }
-      __nanosleep(64);
+    bad_s = 0;
+    if (*poison != 0u) {
+      record_error(err, 106);
+      bad_s = 1;
+    } else {
+      unsigned int* a = arrive + (int64_t)parity * n_heads + hh;
+      const uint64_t t0 = global_ns();
+      while (true) {
+        unsigned int v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+        if ((int)v >= world) break;
+        if (global_ns() - t0 > kWaitLimitNs) {
+          record_error(err, 104);
+          *poison = 1u;
+          __threadfence();
+          bad_s = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
     }
   }
   __syncthreads();
   const unsigned parity = parity_s;
+  const bool bad = bad_s != 0;
   for (int e = threadIdx.x; e < R * dv; e += blockDim.x) {
     const int r = e / dv, d = e - r * dv;
     const int64_t orow = hh * R + r;
@@ -85,7 +105,7 @@ __global__ void xmerge_kernel(float* recv, unsigned int* arrive, unsigned int* s
         A = fmaf(__ldcv(src + 2 + d), sc, A);
       }
     }
-    store_from_float(out, orow * dv + d, out_dtype, M == NEG_INF ? __int_as_float(0x7fc00000) : A / Lsum);
+    store_from_float(out, orow * dv + d, out_dtype, (bad || M == NEG_INF) ? __int_as_float(0x7fc00000) : A / Lsum);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
