@@ -40,6 +40,15 @@ constexpr int kBarConsumers = 1;                 // named barrier id for consume
 constexpr int kSmemLimit = 232448;               // 227 KiB opt-in per CTA on sm_100
 
 // error codes written to the workspace error word
+// Functions off the consumers' per-tile path (segment ends, LUT builds, the producer loop) stay out of
+// line so the hot loop's code is small: instruction fetch is the decode kernel's top stall, and on B200
+// outlining them took the c5 step at T 16384 from 74.6 to 70.3 us (full T: 383.4 to 381.0 us).
+// SUNSHAPE_INLINE_COLD=1 builds inline them again.
+#if defined(SUNSHAPE_INLINE_COLD) && SUNSHAPE_INLINE_COLD
+#define SUNSHAPE_COLD __device__
+#else
+#define SUNSHAPE_COLD __device__ __noinline__
+#endif
 constexpr int kErrWaitFull = 101;
 constexpr int kErrWaitEmpty = 102;
 
@@ -434,7 +443,7 @@ __device__ __forceinline__ void signal_peers(const DecodeParams& p, int64_t hh, 
 // contributors' slot offsets and (when they fit) the gathered slots.  Sums run in the same order as a
 // scalar merge (warps, then contributors in CTA order), so results do not depend on the vector width.
 template <int GP, int DV, int NW, bool PRECISE = false>
-__device__ void finish_segment(const DecodeParams& p, const float* stg, int64_t hh, int64_t tb, int64_t grid,
+SUNSHAPE_COLD void finish_segment(const DecodeParams& p, const float* stg, int64_t hh, int64_t tb, int64_t grid,
                                int ctid, int* flag_s) {
   constexpr int ROWF = DV + 2;
   constexpr int NT = NW * 32;

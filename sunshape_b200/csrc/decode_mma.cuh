@@ -205,7 +205,7 @@ __device__ __forceinline__ void lut_rows_reg(const DecodeParams& p, const float*
 // |q_b . c| <= max_b |q_b| * max_{b,c} |c|, so no entry can overflow; the score is the fp32 sum
 // of the entries times 1 / scale (exact).  The scale is left in *scale_s.
 template <int GP, bool L16>
-__device__ void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
+SUNSHAPE_COLD void build_lut_m(const DecodeParams& p, int64_t hh, const int* perm_s, const int8_t* hslot_s,
                             float* q_s, uint8_t* lut, int ctid, float* scale_s, int kh_lo = 0, int kh_hi = 1 << 20,
                             int c_lo = 0, int c_hi = 1 << 20) {
   c_hi = min(c_hi, p.C);
@@ -619,7 +619,7 @@ void launch_lut_head_block_t(const DecodeParams& prm, int n_heads, cudaStream_t 
 // Producer warp of the tensor-core kernel: TMA tensor boxes for values, bulk
 // copies (+ byte tails) for index and heavy rows, L2 prefetch ahead of the ring.
 template <int DV>
-__device__ void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint64_t* full, uint64_t* empty,
+SUNSHAPE_COLD void produce_mma(const DecodeParams& p, int64_t tb, int64_t te, uint64_t* full, uint64_t* empty,
                             uint8_t* stage0, int n_heavy, int lane, int pid) {
   const int S = p.stages;
   const int64_t hrow = (int64_t)n_heavy * p.bd * (p.heavy_dtype == SUNSHAPE_F32 ? 4 : 2);
