@@ -440,7 +440,10 @@ __global__ void __launch_bounds__(256) lut_cbm_kernel(const __grid_constant__ De
     if (b == 0 && tid < nh) p.lut_scale_global[(int64_t)(s0 + tid) * p.kv_heads + kvh] = 1.f;
   }
   SUNSHAPE_LUTMARK(2);
-  if (c >= p.C) return;
+  if (c >= p.C) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
   const int kh = b >> 3, blo = b & 7;
   constexpr int NH = L16 ? (GP >= 8 ? GP / 8 : 1) : GP / 4;
   int pb[16];
@@ -473,6 +476,29 @@ __global__ void __launch_bounds__(256) lut_cbm_kernel(const __grid_constant__ De
   }
   SUNSHAPE_SPAN_END(1);
   SUNSHAPE_LUTMARK(3);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Launch of a LUT grid as a programmatic dependent of the preceding kernel in the stream.  When that is
+// the previous step's decode_mma_kernel, its CTAs trigger (griddepcontrol.launch_dependents) once their
+// last global-LUT copy has landed, so this grid can overwrite the LUT tables on SMs the decode has
+// already released while its tail merges run.  The LUT kernels end with griddepcontrol.wait: they
+// complete only after the preceding grid, which keeps the next decode's consumers (who wait for this
+// grid) off the workspace and the outputs that the previous decode is still finishing.
+template <typename... Args>
+void launch_pdl(void (*kernel)(Args...), dim3 grid, int threads, size_t smem, cudaStream_t st,
+                const DecodeParams& prm) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, prm);
 }
 
 template <int GP, bool L16>
@@ -493,7 +519,7 @@ void launch_lut_t(const DecodeParams& prm, int n_heads, int n_sms, cudaStream_t 
   const int groups = (batch + hpc - 1) / hpc;
   const int hpc_eff = (batch + groups - 1) / groups;   // what the kernel derives from gridDim.y
   const size_t smem = (size_t)hpc_eff * GP * prm.D * sizeof(float);
-  lut_cbm_kernel<GP, L16><<<dim3(items, groups), 256, smem, st>>>(prm);
+  launch_pdl(lut_cbm_kernel<GP, L16>, dim3(items, groups), 256, smem, st, prm);
 }
 
 // Per-head LUTs for one decode launch, in exactly the shared-memory layout the decode kernel
@@ -505,6 +531,7 @@ template <int GP, bool L16>
 __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ DecodeParams p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   SUNSHAPE_SPAN_START(0);
+  SUNSHAPE_LUTMARK(0);
   __shared__ float q_s[GP * 256];   // this head's query rows, scaled, in model channel order
   __shared__ int perm_s[256];
   __shared__ float red[2];
@@ -556,6 +583,7 @@ __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ Decode
   if (tid < D) perm_s[tid] = pv;
   if (tid == 0) { red[0] = 0.f; red[1] = 1.f; }
   __syncthreads();
+  SUNSHAPE_LUTMARK(1);
   float scale = 1.f;
   if constexpr (L16) {
     float qn = 0.f;
@@ -589,7 +617,10 @@ __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ Decode
   } else {
     if (b == 0 && tid == 0) p.lut_scale_global[hh] = 1.f;
   }
-  if (c >= p.C) return;
+  if (c >= p.C) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
   float v[GP];
 #pragma unroll
   for (int g = 0; g < GP; ++g) v[g] = 0.f;
@@ -609,11 +640,13 @@ __global__ void __launch_bounds__(256) lut_kernel(const __grid_constant__ Decode
                                   : base + (int64_t)kh * NH * kLutC * 128 + blo * 16;
   store_lut_entry<GP, L16>(dst, c, v, scale);
   SUNSHAPE_SPAN_END(1);
+  SUNSHAPE_LUTMARK(2);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 template <int GP, bool L16>
 void launch_lut_head_block_t(const DecodeParams& prm, int n_heads, cudaStream_t st) {
-  lut_kernel<GP, L16><<<dim3(n_heads, prm.nbh * 8), 256, 0, st>>>(prm);
+  launch_pdl(lut_kernel<GP, L16>, dim3(n_heads, prm.nbh * 8), 256, 0, st, prm);
 }
 
 // Producer warp of the tensor-core kernel: TMA tensor boxes for values, bulk
@@ -826,6 +859,8 @@ __global__ void __launch_bounds__(kThreadsM, 1) decode_mma_kernel(const __grid_c
       build_lut_m<GP, L16>(p, hh, perm_s, hslot_s, q_s, lut, ctid, scale_s);
       if (L16) inv_scale = scale_s[0];
     }
+    // this CTA reads no more global LUT tables: the next LUT grid may start overwriting them
+    if (fend >= te) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 #ifdef SUNSHAPE_TRACE
     if (ctid == 0 && f - tb < 2 * p.tph && (hh - tb / p.tph) < 2) SUNSHAPE_MARK(4 + 2 * (int)(hh - tb / p.tph));
 #endif
